@@ -1,0 +1,136 @@
+// Tensor-parallel collectives for backend-cuda: one NCCL communicator per
+// device, collectives enqueued on the device stream (so they order with the
+// kernels and can sit inside a captured CUDA graph).
+//
+// NCCL is loaded at run time with dlopen("libnccl.so.2"): when the host
+// process already carries an NCCL (PyTorch bundles one) the same library is
+// reused, and the product library has no link-time NCCL dependency.
+// The reference has no distributed communication at all (README.md:107);
+// this is the Megatron-style tensor parallelism the llama-dense layer
+// admits: an all-reduce after the row-parallel o/down projections and an
+// all-gather of vocabulary-split logits.
+#include <dlfcn.h>
+#include <nccl.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "device_internal.h"
+#include "kernels/kernels.h"
+
+namespace {
+
+struct NcclApi {
+    void *handle = nullptr;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                               ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+    bool ok = false;
+};
+
+NcclApi &api() {
+    static NcclApi a;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        const char *names[] = {"libnccl.so.2", "libnccl.so"};
+        for (const char *n : names) {
+            a.handle = dlopen(n, RTLD_NOW | RTLD_GLOBAL);
+            if (a.handle) break;
+        }
+        if (!a.handle) return;
+        a.get_unique_id = (decltype(a.get_unique_id))dlsym(a.handle, "ncclGetUniqueId");
+        a.init_rank = (decltype(a.init_rank))dlsym(a.handle, "ncclCommInitRank");
+        a.all_reduce = (decltype(a.all_reduce))dlsym(a.handle, "ncclAllReduce");
+        a.all_gather = (decltype(a.all_gather))dlsym(a.handle, "ncclAllGather");
+        a.destroy = (decltype(a.destroy))dlsym(a.handle, "ncclCommDestroy");
+        a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.all_gather && a.destroy;
+    });
+    return a;
+}
+
+}  // namespace
+
+struct CommState {
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1;
+};
+
+extern "C" int slc_comm_unique_id(uint8_t out_id[128]) {
+    if (!out_id) return SLC_ERR_EXECUTION;
+    NcclApi &a = api();
+    if (!a.ok) return SLC_ERR_UNIMPLEMENTED;
+    ncclUniqueId id;
+    if (a.get_unique_id(&id) != ncclSuccess) return SLC_ERR_EXECUTION;
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    memcpy(out_id, &id, 128);
+    return SLC_OK;
+}
+
+extern "C" int slc_comm_init(slc_device *d, const uint8_t unique_id[128], int rank, int world) {
+    if (!d || !unique_id) return SLC_ERR_EXECUTION;
+    if (world < 1 || rank < 0 || rank >= world) return slc_fail(d, SLC_ERR_EXECUTION, "invalid rank");
+    NcclApi &a = api();
+    if (!a.ok) return slc_fail(d, SLC_ERR_UNIMPLEMENTED, "libnccl.so.2 could not be loaded");
+    release_comm(d);
+    ncclUniqueId id;
+    memcpy(&id, unique_id, 128);
+    cudaSetDevice(d->ordinal);
+    CommState *c = new CommState();
+    c->rank = rank;
+    c->world = world;
+    if (a.init_rank(&c->comm, world, id, rank) != ncclSuccess) {
+        delete c;
+        return slc_fail(d, SLC_ERR_EXECUTION, "ncclCommInitRank failed");
+    }
+    d->comm = c;
+    return SLC_OK;
+}
+
+extern "C" int slc_comm_world(const slc_device *d, int *rank, int *world) {
+    if (!d) return SLC_ERR_EXECUTION;
+    if (rank) *rank = d->comm ? d->comm->rank : 0;
+    if (world) *world = d->comm ? d->comm->world : 1;
+    return SLC_OK;
+}
+
+void release_comm(slc_device *d) {
+    if (!d->comm) return;
+    if (d->comm->comm && api().ok) api().destroy(d->comm->comm);
+    delete d->comm;
+    d->comm = nullptr;
+}
+
+int comm_all_reduce(slc_device *d, float *data, uint64_t count) {
+    if (!d->comm) return SLC_ERR_EXECUTION;
+    if (count == 0 || d->comm->world == 1) return SLC_OK;
+    ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, d->comm->comm,
+                                      d->stream);
+    slc::k::count_launch();
+    return r == ncclSuccess ? SLC_OK : SLC_ERR_EXECUTION;
+}
+
+int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, uint64_t cols) {
+    if (!d->comm) return SLC_ERR_EXECUTION;
+    const uint64_t world = (uint64_t)d->comm->world;
+    if (rows == 0 || cols == 0) return SLC_OK;
+    if (world == 1) return slc::k::copy_f32(d->stream, in, out, rows * cols) == cudaSuccess
+                              ? SLC_OK : SLC_ERR_EXECUTION;
+    // NCCL gathers rank blocks contiguously ([world][rows][cols]); with one
+    // row that already is [rows, world * cols], otherwise interleave.
+    // Staging after the GEMV tickets, inside the kernel-scratch region.
+    const uint64_t ticket_bytes = 64 * 1024 * sizeof(unsigned);
+    float *dst = rows == 1 ? out : reinterpret_cast<float *>(d->workspace + ticket_bytes);
+    if (rows > 1 && world * rows * cols * sizeof(float) > d->workspace_bytes / 2 - ticket_bytes)
+        return SLC_ERR_EXECUTION;
+    ncclResult_t r = api().all_gather(in, dst, rows * cols, ncclFloat32, d->comm->comm, d->stream);
+    slc::k::count_launch();
+    if (r != ncclSuccess) return SLC_ERR_EXECUTION;
+    if (rows > 1 &&
+        slc::k::interleave_blocks(d->stream, dst, out, world, rows, cols) != cudaSuccess)
+        return SLC_ERR_EXECUTION;
+    return SLC_OK;
+}

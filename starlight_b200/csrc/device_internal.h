@@ -1,0 +1,71 @@
+// Internal state of a backend-cuda device (not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/starlight_cuda.h"
+#include "kernels/kernels.h"
+
+struct DeviceBuffer {
+    void *alloc = nullptr;  // cudaMalloc result
+    char *ptr = nullptr;    // aligned start of element 0
+    uint64_t elements = 0;
+    bool u32 = false;
+    std::vector<uint32_t> shadow;  // host copy of a U32 buffer (written only by upload)
+};
+
+struct QuantBinding {
+    uint32_t scales;
+    uint32_t format;
+    uint32_t group;
+};
+
+struct CaptureState;  // command capture and graph replay (capture.cpp)
+struct CommState;     // NCCL communicator (comm.cpp)
+
+struct slc_device {
+    int ordinal = 0;
+    cudaStream_t stream = nullptr;
+    std::vector<DeviceBuffer> buffers;
+    std::unordered_map<uint32_t, QuantBinding> quant;
+    char *workspace = nullptr;
+    uint64_t workspace_bytes = 0;
+    char *staging = nullptr;
+    uint64_t staging_bytes = 0;
+    uint32_t *device_flag = nullptr;
+    slc_error last{};
+    CaptureState *capture = nullptr;
+    CommState *comm = nullptr;
+};
+
+// Error helpers shared by the operator layer.
+int slc_fail(slc_device *d, int status, const char *msg);
+int slc_fail_buffer(slc_device *d, uint32_t buffer);
+int slc_fail_range(slc_device *d, uint32_t buffer, uint64_t offset, uint64_t len);
+int slc_quant_view(slc_device *d, uint32_t codes_buffer, uint64_t offset_words, uint64_t rows,
+                   uint64_t k, uint32_t format, uint32_t group, slc::k::QuantWeight *w);
+
+// Capture hooks: flush_capture launches any recorded-but-unlaunched work (a
+// no-op when capture is off) and must run before any host-visible effect.
+int flush_capture(slc_device *d);
+void release_capture(slc_device *d);
+// Launch one validated command (used by the capture layer when replaying
+// eagerly). Returns an slc_status.
+int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
+                       const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
+                       const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
+                       uint64_t n_scalars);
+// Try to record a validated command for graph replay. Returns 1 if the
+// command was recorded (launch deferred), 0 if it must be launched now.
+int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
+                   const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
+                   const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
+                   uint64_t n_scalars);
+
+// NCCL hooks (comm.cpp).
+void release_comm(slc_device *d);
+int comm_all_reduce(slc_device *d, float *data, uint64_t count);
+int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, uint64_t cols);

@@ -1,0 +1,106 @@
+// Host-side launchers of the backend-cuda kernels. Every launcher enqueues
+// on `stream`, performs no allocation and returns the launch status.
+// Shapes have been validated by the device layer before any call.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace slc {
+namespace k {
+
+// ---- elementwise (elementwise.cu) ------------------------------------------
+cudaError_t add(cudaStream_t s, const float *a, const float *b, float *out, size_t n);
+cudaError_t mul(cudaStream_t s, const float *a, const float *b, float *out, size_t n);
+cudaError_t scale(cudaStream_t s, const float *x, float factor, float *out, size_t n);
+cudaError_t silu(cudaStream_t s, const float *x, float *out, size_t n);
+// out = silu(a) * b (SwiGLU gate epilogue).
+cudaError_t silu_mul(cudaStream_t s, const float *a, const float *b, float *out, size_t n);
+// out[r, c] = a[r, c] + b[r, c] + bias[c]  (residual add with a broadcast bias)
+cudaError_t add_bias(cudaStream_t s, const float *a, const float *b, const float *bias,
+                     float *out, size_t rows, size_t cols);
+cudaError_t copy_f32(cudaStream_t s, const float *src, float *dst, size_t n);
+
+// ---- reductions (norm.cu, softmax.cu) --------------------------------------
+cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out, size_t rows,
+                     size_t hidden, float eps);
+cudaError_t softmax(cudaStream_t s, const float *x, float *out, size_t rows, size_t cols);
+cudaError_t softmax_causal(cudaStream_t s, const float *x, float *out, size_t rows, size_t cols,
+                           size_t seq, size_t past_len);
+
+// ---- rope.cu ----------------------------------------------------------------
+cudaError_t rope(cudaStream_t s, const float *x, const uint32_t *positions, float *out,
+                 size_t batch, size_t heads, size_t seq, size_t head_dim, float theta,
+                 int gptj);
+
+// ---- layout.cu ---------------------------------------------------------------
+cudaError_t gather(cudaStream_t s, const float *table, const uint32_t *ids, float *out,
+                   size_t vocab, size_t hidden, size_t rows, uint32_t *error_flag);
+cudaError_t last_token(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
+                       size_t hidden, size_t seq_len);
+cudaError_t split_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
+                        size_t heads, size_t head_dim);
+cudaError_t merge_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
+                        size_t heads, size_t head_dim);
+// dst[r, b * cols + c] = src[b, r, c] for b < blocks (rank blocks -> rows).
+cudaError_t interleave_blocks(cudaStream_t s, const float *src, float *dst, size_t blocks,
+                              size_t rows, size_t cols);
+
+// ---- attention.cu --------------------------------------------------------------
+struct KvGeometry {
+    size_t batch, layers, layer, kv_heads, head_dim, max_seq;
+};
+cudaError_t kv_append(cudaStream_t s, const float *k, const float *v, float *cache,
+                      const KvGeometry &g, size_t past_len, size_t seq);
+// Workspace needed by causal_attention for the given shape (bytes).
+size_t attention_workspace_bytes(size_t batch, size_t heads, size_t kv_heads, size_t seq,
+                                 size_t past_len, size_t head_dim);
+cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, const float *v,
+                             float *cache, float *out, const KvGeometry &g, size_t heads,
+                             size_t seq, size_t past_len, float scale, void *workspace,
+                             size_t workspace_bytes);
+
+// ---- matmul_f32.cu --------------------------------------------------------------
+// out[b] = a[b or 0] . w[b or 0]^T (NT) or a . w (NN), batch broadcast when a
+// batch count is 1 (device.rs:1301-1407).
+cudaError_t matmul_f32(cudaStream_t s, const float *a, const float *w, float *out,
+                       size_t batch_a, size_t batch_b, size_t m, size_t k, size_t n,
+                       bool transposed);
+
+// ---- gemv_quant.cu ---------------------------------------------------------------
+struct QuantWeight {
+    const uint8_t *codes;  // payload, rows of row_bytes
+    const float *scales;   // [n, groups]
+    size_t n, k, group, groups, row_bytes;
+    int format;            // 0 INT4, 1 INT8
+};
+// Tiled SIMT GEMM with the weight dequantized on load (prefill-sized m).
+cudaError_t qgemm_f32(cudaStream_t s, const float *a, size_t m, const QuantWeight &w, float *out);
+size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m);
+// out[m, n] = x[m, k] . dequant(w)[n, k]^T
+cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                    void *workspace, size_t workspace_bytes);
+cudaError_t quantize(cudaStream_t s, const float *w, size_t n, size_t k, size_t group,
+                     int format, uint8_t *codes, float *scales);
+cudaError_t dequantize(cudaStream_t s, const QuantWeight &w, float *out);
+
+// ---- fused (fused.cu) -------------------------------------------------------------
+// Row-wise inverse RMS of x: inv[r] = 1 / sqrt(mean(x[r]^2) + eps).
+cudaError_t rms_inverse(cudaStream_t s, const float *x, float *inv, size_t rows, size_t hidden,
+                        float eps);
+// y[r, i] = (x[r, i] * inv[r]) * w[i]
+cudaError_t rms_apply(cudaStream_t s, const float *x, const float *inv, const float *w,
+                      float *out, size_t rows, size_t hidden);
+
+// ---- init.cu ----------------------------------------------------------------
+// out[i] = N(mean, std) draw number offset + i of the stream `seed`.
+cudaError_t fill_normal(cudaStream_t s, float *out, size_t n, uint64_t seed, uint64_t offset,
+                        float mean, float std);
+
+// Launch counter (incremented by every launcher).
+uint64_t launch_count();
+void count_launch();
+
+}  // namespace k
+}  // namespace slc

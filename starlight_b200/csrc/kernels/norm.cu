@@ -1,0 +1,176 @@
+// RMSNorm (crates/backends/backend-cpu/src/reference/norm.rs:27-60):
+//   out = x * (1 / sqrt(sum(x^2) / hidden + eps)) * weight
+//
+// HBM-bound: algorithmic bytes 8 * rows * hidden + 4 * hidden. A row is read
+// from HBM once: it is held in registers (128-bit loads) while the sum of
+// squares is reduced (warp shuffles, then shared memory across warps), and
+// written once with streaming stores. The reciprocal square root is one IEEE
+// sqrt and one IEEE division, and each element is scaled by exactly two
+// rounded multiplies in the reference's order, so results differ from the
+// reference only through the order of the sum of squares.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace slc {
+namespace k {
+namespace {
+
+__device__ __forceinline__ float inv_rms(float sum_sq, size_t hidden, float eps) {
+    float mean = __fdiv_rn(sum_sq, (float)hidden);
+    return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
+}
+
+// One CTA of 256 threads per row, NV float4 per thread kept in registers.
+template <int NV>
+__global__ void __launch_bounds__(256) rms_norm_regs(const float *__restrict__ x,
+                                                     const float *__restrict__ w,
+                                                     float *__restrict__ out, size_t rows,
+                                                     size_t hidden, float eps) {
+    __shared__ float partial[8];
+    const size_t h4 = hidden / 4;
+    for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float *xr = x + row * hidden;
+        float4 v[NV];
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            size_t c = threadIdx.x + (size_t)i * 256;
+            if (c < h4) {
+                v[i] = ld_stream_f4(xr + 4 * c);
+                ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
+            }
+        }
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float total = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) total += partial[i];
+        float inv = inv_rms(total, hidden, eps);
+        float *orow = out + row * hidden;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            size_t c = threadIdx.x + (size_t)i * 256;
+            if (c < h4) {
+                float4 g = *reinterpret_cast<const float4 *>(w + 4 * c);
+                float4 r = make_float4(__fmul_rn(__fmul_rn(v[i].x, inv), g.x),
+                                       __fmul_rn(__fmul_rn(v[i].y, inv), g.y),
+                                       __fmul_rn(__fmul_rn(v[i].z, inv), g.z),
+                                       __fmul_rn(__fmul_rn(v[i].w, inv), g.w));
+                st_stream_f4(orow + 4 * c, r);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// One warp per row for short rows (hidden <= 1024): many rows per CTA.
+__global__ void __launch_bounds__(256) rms_norm_warp(const float *__restrict__ x,
+                                                     const float *__restrict__ w,
+                                                     float *__restrict__ out, size_t rows,
+                                                     size_t hidden, float eps) {
+    const int lane = threadIdx.x & 31;
+    size_t warps = (size_t)gridDim.x * 8;
+    for (size_t row = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += warps) {
+        const float *xr = x + row * hidden;
+        float ss = 0.f;
+        for (size_t c = lane; c < hidden; c += 32) ss += xr[c] * xr[c];
+        float inv = inv_rms(warp_sum(ss), hidden, eps);
+        float *orow = out + row * hidden;
+        for (size_t c = lane; c < hidden; c += 32) orow[c] = __fmul_rn(__fmul_rn(xr[c], inv), w[c]);
+    }
+}
+
+// Generic: one CTA per row, two passes (re-read from L2) for very wide rows.
+__global__ void __launch_bounds__(256) rms_norm_generic(const float *__restrict__ x,
+                                                        const float *__restrict__ w,
+                                                        float *__restrict__ out, size_t rows,
+                                                        size_t hidden, float eps) {
+    __shared__ float partial[8];
+    for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
+        const float *xr = x + row * hidden;
+        float ss = 0.f;
+        for (size_t c = threadIdx.x; c < hidden; c += 256) ss += xr[c] * xr[c];
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        float total = 0.f;
+        for (int i = 0; i < 8; i++) total += partial[i];
+        float inv = inv_rms(total, hidden, eps);
+        float *orow = out + row * hidden;
+        for (size_t c = threadIdx.x; c < hidden; c += 256)
+            orow[c] = __fmul_rn(__fmul_rn(xr[c], inv), w[c]);
+        __syncthreads();
+    }
+}
+
+// Inverse RMS only (prologue of the fused RmsNorm x MatMul path).
+__global__ void __launch_bounds__(256) rms_inverse_kernel(const float *__restrict__ x,
+                                                          float *__restrict__ inv, size_t rows,
+                                                          size_t hidden, float eps) {
+    const int lane = threadIdx.x & 31;
+    size_t warps = (size_t)gridDim.x * 8;
+    for (size_t row = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += warps) {
+        const float *xr = x + row * hidden;
+        float ss = 0.f;
+        for (size_t c = lane; c < hidden; c += 32) ss += xr[c] * xr[c];
+        float r = inv_rms(warp_sum(ss), hidden, eps);
+        if (lane == 0) inv[row] = r;
+    }
+}
+
+__global__ void __launch_bounds__(256) rms_apply_kernel(const float *__restrict__ x,
+                                                        const float *__restrict__ inv,
+                                                        const float *__restrict__ w,
+                                                        float *__restrict__ out, size_t rows,
+                                                        size_t hidden) {
+    size_t n = rows * hidden, stride = (size_t)gridDim.x * blockDim.x;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        size_t r = i / hidden, c = i - r * hidden;
+        out[i] = __fmul_rn(__fmul_rn(x[i], inv[r]), w[c]);
+    }
+}
+
+}  // namespace
+
+cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out, size_t rows,
+                     size_t hidden, float eps) {
+    if (rows == 0) return cudaSuccess;
+    bool vec = hidden % 4 == 0 && aligned16(x) && aligned16(w) && aligned16(out);
+    size_t h4 = hidden / 4;
+    int grid = (int)(rows < (size_t)kSmCount * 16 ? rows : (size_t)kSmCount * 16);
+    if (hidden <= 1024 && rows >= 64) {
+        rms_norm_warp<<<grid_for(rows, 8, 16), 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    } else if (vec && h4 <= 256) {
+        rms_norm_regs<1><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    } else if (vec && h4 <= 512) {
+        rms_norm_regs<2><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    } else if (vec && h4 <= 1024) {
+        rms_norm_regs<4><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    } else if (vec && h4 <= 2048) {
+        rms_norm_regs<8><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    } else {
+        rms_norm_generic<<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rms_inverse(cudaStream_t s, const float *x, float *inv, size_t rows, size_t hidden,
+                        float eps) {
+    if (rows == 0) return cudaSuccess;
+    rms_inverse_kernel<<<grid_for(rows, 8, 16), 256, 0, s>>>(x, inv, rows, hidden, eps);
+    count_launch();
+    return cudaGetLastError();
+}
+
+cudaError_t rms_apply(cudaStream_t s, const float *x, const float *inv, const float *w,
+                      float *out, size_t rows, size_t hidden) {
+    if (rows == 0) return cudaSuccess;
+    rms_apply_kernel<<<grid_for(rows * hidden, 256), 256, 0, s>>>(x, inv, w, out, rows, hidden);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace k
+}  // namespace slc
