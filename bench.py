@@ -1,0 +1,449 @@
+#!/usr/bin/env python
+"""Benchmark of the backend-cuda hot path: Llama-3-8B-shaped INT4 decode.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Workload: llama-dense, 32 layers, hidden 4096, 32/8
+heads x 128, FFN 14336, vocab 128256, RoPE theta 5e5, weights N(0, 0.02)
+quantized to symmetric INT4 group 128 (generated on the device), f32
+activations and KV cache, a 1024-token random prompt (prefill, untimed), then
+greedy decode. One timed step = one decode token per sequence through
+Engine::step (slc_llama_step): every command of the decode program goes
+through slc_dispatch. With N > 1 (torchrun) the model is tensor-parallel over
+N GPUs (NCCL all-reduce after o/down, all-gather of the logits); the total
+work is fixed, so scaling is "strong".
+
+Reported: `value` = decode tok/s from the device time of the steps (CUDA
+events on the device stream, max over ranks); `e2e` = the same through the
+public API with host buffers (ids/positions uploaded, logits downloaded every
+step, host wall clock, max over ranks); `roofline` = the INT4 decode GEMV
+(the dominant kernel) measured live on the model's own weights;
+`cpu_baseline` = the CPU oracle (the restated reference kernels) on this
+host's cores. The weights streamed per step (~4 GB) exceed the 126 MB L2, so
+no flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode tok/s (Llama-3-8B-shaped llama-dense, INT4 g128)"
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemv_int4_decode_8b.md")
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=32)
+    ap.add_argument("--warmup", type=int, default=4)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--layers", type=int, default=32, help="(testing only) fewer layers")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ---------------------------------------------------------------- helpers --
+
+def hbm_peak():
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """DRAM bytes per launch of the GEMV from the committed ncu summary, if any."""
+    try:
+        for line in open(TRAFFIC_PROFILE):
+            if line.strip().startswith("traffic_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].strip().split()[0])
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        loaded = [v for v in sm if v > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "reasons": reasons, "samples": len(rows)}
+
+
+class Dist:
+    """One process per GPU; gloo for host plumbing (ids broadcast, timing max)."""
+
+    def __init__(self, gpus: int):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            self.pg = dist
+        if self.world != gpus and gpus != 1:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}")
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64)
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def broadcast_bytes(self, data: bytes | None, n: int) -> bytes:
+        if not self.pg:
+            return data
+        import torch
+        t = torch.zeros(n, dtype=torch.uint8)
+        if self.rank == 0:
+            t[:] = torch.frombuffer(bytearray(data), dtype=torch.uint8)
+        self.pg.broadcast(t, 0)
+        return bytes(t.numpy().tobytes())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+def emit(line: dict):
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------- CPU (oracle) arm --
+
+def oracle_decode_sample(batch: int, prompt: int, threads: int):
+    """Per-token time of the CPU reference path for the 8B decode step, from a
+    bounded sample: one decoder layer's kernels (7 matmul_nt against f32
+    weights, the reference's dequantize-then-matmul path; causal_attention over
+    the prompt; 2 rms_norm, rope, add) timed once and multiplied by 32 layers,
+    plus matmul_nt against an 8192-row slice of lm_head scaled to 128256 rows.
+    Returns (seconds per token, description)."""
+    from oracle import pyoracle as orc
+    orc.set_threads(threads)
+    H, Hq, Hkv, D, I, V = 4096, 32, 8, 128, 14336, 128256
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((batch, H), dtype=np.float32)
+    shapes = [(Hq * D, H), (Hkv * D, H), (Hkv * D, H), (H, Hq * D), (I, H), (I, H), (H, I)]
+    ws = [(rng.standard_normal(n * k, dtype=np.float32) * 0.02) for n, k in shapes]
+    max_seq = prompt + 1
+    cache = rng.standard_normal(batch * 1 * 2 * max_seq * Hkv * D, dtype=np.float32)
+    q = rng.standard_normal(batch * Hq * D, dtype=np.float32)
+    kv = rng.standard_normal(batch * Hkv * D, dtype=np.float32)
+    head = rng.standard_normal(8192 * H, dtype=np.float32) * 0.02
+    g = np.ones(H, np.float32)
+    t0 = time.perf_counter()
+    for (n, k), w in zip(shapes, ws):
+        xi = x if k == H else rng.standard_normal((batch, k), dtype=np.float32)
+        orc.matmul_nt(xi, w, 1, batch, k, n)
+    orc.causal_attention(q, kv, kv, cache, batch, 1, 0, Hq, Hkv, 1, prompt, D, max_seq,
+                         1.0 / np.sqrt(D))
+    for _ in range(2):
+        orc.rms_norm(x, g, batch, H, 1e-5)
+    orc.rope(q, np.full(batch, prompt, np.uint32), batch, Hq, 1, D, 500000.0)
+    orc.add(x, x, batch * H)
+    layer = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    orc.matmul_nt(x, head, 1, batch, H, 8192)
+    head_t = (time.perf_counter() - t1) * (V / 8192)
+    per_token = 32 * layer + head_t
+    desc = (f"one 8B decoder layer (7 matmul_nt, causal_attention over {prompt} keys, norms, "
+            f"rope, add) x 32 + lm_head slice 8192/128256 rows scaled; batch {batch}; "
+            f"restated reference kernels, {threads} OpenMP threads")
+    return per_token, desc
+
+
+def run_reference(args, dist: Dist):
+    if dist.rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    samples = []
+    for _ in range(max(args.warmup, 0)):
+        oracle_decode_sample(args.batch, args.prompt, threads)
+    for _ in range(args.steps):
+        t, desc = oracle_decode_sample(args.batch, args.prompt, threads)
+        samples.append(t)
+    per_token = statistics.mean(samples)
+    value = args.batch / per_token
+    emit({"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+          "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_token * 1e3,
+          "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+          "data": "synthetic", "impl": "reference",
+          "config": {"workload": "llama3-8b-int4-decode", "batch": args.batch,
+                     "prompt": args.prompt, "parallelism": "cpu"},
+          "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
+                           "sample": desc},
+          "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0,
+                  "d2h_bytes_per_step": 0}})
+    return 0
+
+
+# ------------------------------------------------------------ GPU arm ------
+
+def _gemv_roofline(dev, model, cfg, batch, peak):
+    """Live measurement of the INT4 decode GEMV (MatMulNT, M = batch) on the
+    model's own quantized weights, every layer in turn (working set ~4 GB, cold
+    in L2). Algorithmic bytes per launch: N*K/2 codes + 4*N*K/128 scales +
+    4*M*(K+N) activations."""
+    import torch
+    from starlight_b200.device import BufferRef, Op, OpCode, Value
+    stream = torch.cuda.ExternalStream(dev.stream())
+    roles = ["q", "k", "v", "o", "gate", "up", "down"]
+    launches = []
+    xbufs = {}
+    for role in roles + ["lm_head"]:
+        ref, val = model.weight_ref(role, 0)
+        n, k = val.shape
+        if k not in xbufs:
+            b = dev.allocate_f32(batch * k)
+            dev.upload_f32(b, np.random.default_rng(k).standard_normal(batch * k, dtype=np.float32))
+            xbufs[k] = b
+    outs = {}
+    for role in roles + ["lm_head"]:
+        _, val = model.weight_ref(role, 0)
+        n = val.shape[0]
+        if n not in outs:
+            outs[n] = dev.allocate_f32(batch * n)
+    for layer in range(cfg.layers):
+        for role in roles:
+            launches.append(model.weight_ref(role, layer))
+    launches.append(model.weight_ref("lm_head", 0))
+
+    def run_all():
+        for ref, val in launches:
+            n, k = val.shape
+            dev.dispatch(Op(OpCode.MatMulNT), [BufferRef(xbufs[k], 0, batch * k), ref],
+                         [Value.f32((batch, k)), val], [BufferRef(outs[n], 0, batch * n)],
+                         [Value.f32((batch, n))])
+
+    run_all()
+    dev.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 3
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(reps):
+            run_all()
+        t1.record(stream)
+    dev.synchronize()
+    t1.synchronize()
+    ms = t0.elapsed_time(t1)
+    total_bytes = 0
+    for ref, val in launches:
+        n, k = val.shape
+        total_bytes += n * k // 2 + 4 * n * (k // 128) + 4 * batch * (k + n)
+    n_launch = len(launches)
+    per_launch_bytes = total_bytes / n_launch
+    per_launch_s = ms / 1e3 / (reps * n_launch)
+    achieved = per_launch_bytes / per_launch_s / 1e9
+    traffic = profile_traffic()
+    return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
+            "frac": achieved / peak[0], "traffic": traffic,
+            "kernel": "qgemv_mma<INT4> (MatMulNT, M=%d) over one decode step's weight mix" % batch,
+            "algorithmic_bytes_per_launch": per_launch_bytes, "launch_us": per_launch_s * 1e6,
+            "peak_source": peak[1]}
+
+
+def rmsnorm_gbs(dev, peak):
+    """RMSNorm over [4096, 4096] f32 (64 MiB in, 64 MiB out), 8 distinct
+    inputs rotated so that every launch reads from HBM."""
+    import torch
+    from starlight_b200.device import BufferRef, Op, OpCode, Value, ValueRole
+    rows, h = 4096, 4096
+    stream = torch.cuda.ExternalStream(dev.stream())
+    xs = [dev.allocate_f32(rows * h) for _ in range(8)]
+    rng = np.random.default_rng(3)
+    for b in xs:
+        dev.upload_f32(b, rng.standard_normal(rows * h, dtype=np.float32))
+    w = dev.allocate_f32(h)
+    dev.upload_f32(w, 1.0 + 0.1 * rng.standard_normal(h, dtype=np.float32))
+    outs = [dev.allocate_f32(rows * h) for _ in range(2)]
+    op = Op(OpCode.RmsNorm, eps=1e-5)
+
+    def one(i):
+        dev.dispatch(op, [BufferRef(xs[i % 8], 0, rows * h), BufferRef(w, 0, h)],
+                     [Value.f32((rows, h)), Value.f32((h,), ValueRole.Param)],
+                     [BufferRef(outs[i % 2], 0, rows * h)], [Value.f32((rows, h))])
+
+    for i in range(4):
+        one(i)
+    dev.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 32
+    t0.record(stream)
+    for i in range(reps):
+        one(i)
+    t1.record(stream)
+    dev.synchronize()
+    t1.synchronize()
+    s = t0.elapsed_time(t1) / 1e3 / reps
+    bytes_ = 8 * rows * h + 4 * h
+    return {"shape": [rows, h], "achieved_gbs": bytes_ / s / 1e9,
+            "frac": bytes_ / s / 1e9 / peak[0], "launch_us": s * 1e6}
+
+
+def run_ours(args, dist: Dist):
+    import torch
+    from starlight_b200.device import CudaDevice, comm_unique_id
+    from starlight_b200.engine import DECODE, PREFILL, LLAMA3_8B, Llama, LlamaConfig
+
+    world, rank = dist.world, dist.rank
+    torch.cuda.set_device(dist.local)
+    dev = CudaDevice(dist.local)
+    if world > 1:
+        uid = comm_unique_id() if rank == 0 else None
+        uid = dist.broadcast_bytes(uid, 128)
+        dev.comm_init(uid, rank, world)
+    B, T = args.batch, args.prompt
+    max_seq = T + args.warmup + args.steps + 8
+    cfg = LlamaConfig(**{**LLAMA3_8B.__dict__, "batch": B, "prefill_len": T, "max_seq": max_seq,
+                         "layers": args.layers, "tp_rank": rank, "tp_world": world})
+    model = Llama(dev, cfg)
+    model.init_random(seed=8, std=0.02)
+    V = cfg.vocab
+    rng = np.random.default_rng(1234)
+    prompt = rng.integers(0, V, size=B * T, dtype=np.uint32)
+    pos = np.tile(np.arange(T, dtype=np.uint32), B)
+    logits = model.step(PREFILL, prompt, pos, T, 0)
+    ids = logits.argmax(axis=1).astype(np.uint32)
+    past = T
+    for _ in range(args.warmup):
+        logits = model.step(DECODE, ids, np.full(B, past, np.uint32), 1, past)
+        ids = logits.argmax(axis=1).astype(np.uint32)
+        past += 1
+
+    sampler = ClockSampler(dist.local)
+    sampler.start()
+    launches0 = dev.launch_count()
+    dist.barrier()
+    dev.synchronize()
+    device_ms = 0.0
+    w0 = time.perf_counter()
+    for _ in range(args.steps):
+        logits = model.step(DECODE, ids, np.full(B, past, np.uint32), 1, past)
+        device_ms += model.last_step_ms()
+        ids = logits.argmax(axis=1).astype(np.uint32)
+        past += 1
+    dev.synchronize()
+    wall = time.perf_counter() - w0
+    dist.barrier()
+    launches = dev.launch_count() - launches0
+    clocks = sampler.stop()
+    device_ms = dist.max(device_ms)
+    wall = dist.max(wall)
+
+    result = None
+    if rank == 0:
+        peak = hbm_peak()
+        roof = _gemv_roofline(dev, model, cfg, B, peak) if world == 1 else None
+        norm = rmsnorm_gbs(dev, peak) if world == 1 else None
+        value = B * args.steps / (device_ms / 1e3)
+        e2e = B * args.steps / wall
+        result = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": device_ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 activations, int4 weights", "data": "synthetic",
+            "config": {"workload": "llama3-8b-int4-decode", "model": "llama-dense 8B shape",
+                       "batch": B, "prompt": T, "layers": cfg.layers, "quant": "int4 g128",
+                       "global_batch": B, "seq_len": T,
+                       "parallelism": f"tp{world}" if world > 1 else "single",
+                       "l2": "no flush: ~4 GB of weights streamed per step (> 126 MB L2)",
+                       "commands_per_step": model.command_count(DECODE)},
+            "clocks": clocks,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * 4 * B,
+                    "d2h_bytes_per_step": 4 * B * V},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "norm": norm,
+            "weight_bytes_per_rank": model.weight_bytes(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            threads = os.cpu_count() or 1
+            per_token, desc = oracle_decode_sample(B, T, threads)
+            result["cpu_baseline"] = {"value": B / per_token, "unit": "tok/s", "cores": threads,
+                                      "kind": "port", "sample": desc}
+    model.close()
+    dev.close()
+    return result
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    dist = Dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, dist)
+        result = run_ours(args, dist)
+        if result is not None:
+            emit(result)
+        return 0
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

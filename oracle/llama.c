@@ -39,6 +39,7 @@ enum {
 
 typedef struct {
     float *w;          /* f32 weight (dequantized when quantized) */
+    float *src;        /* the weight before quantization (quantized roles) */
     uint8_t *codes;    /* quantized payload or NULL */
     float *scales;
     size_t rows, cols; /* logical [rows, cols]; 1-D weights have rows == 1 */
@@ -91,6 +92,7 @@ orc_llama *orc_llama_create(const orc_llama_config *cfg) {
             weight_t *w = &m->weights[slot_of(m, role, l)];
             role_shape(cfg, role, &w->rows, &w->cols);
             w->w = (float *)calloc(w->rows * w->cols, sizeof(float));
+            w->src = (float *)calloc(w->rows * w->cols, sizeof(float));
             if (cfg->quant_format >= 0 && is_matrix_role(role)) {
                 w->codes = (uint8_t *)calloc(w->rows * orc_quant_row_bytes(cfg->quant_format, w->cols), 1);
                 w->scales = (float *)calloc(w->rows * orc_quant_groups(w->cols, cfg->group_size), sizeof(float));
@@ -106,6 +108,7 @@ void orc_llama_destroy(orc_llama *m) {
     if (!m) return;
     for (size_t i = 0; i < m->nslots; i++) {
         free(m->weights[i].w);
+        free(m->weights[i].src);
         free(m->weights[i].codes);
         free(m->weights[i].scales);
     }
@@ -123,6 +126,10 @@ float *orc_llama_weight(orc_llama *m, int role, uint32_t layer) {
     return m->weights[slot_of(m, role, layer)].w;
 }
 
+const float *orc_llama_weight_source(const orc_llama *m, int role, uint32_t layer) {
+    return m->weights[slot_of(m, role, layer)].src;
+}
+
 const uint8_t *orc_llama_codes(const orc_llama *m, int role, uint32_t layer) {
     return m->weights[slot_of(m, role, layer)].codes;
 }
@@ -132,6 +139,7 @@ const float *orc_llama_scales(const orc_llama *m, int role, uint32_t layer) {
 }
 
 static void finish_weight(orc_llama *m, weight_t *w) {
+    memcpy(w->src, w->w, w->rows * w->cols * sizeof(float));
     if (!w->codes) return;
     orc_quantize(m->cfg.quant_format, w->w, w->rows, w->cols, m->cfg.group_size,
                  w->codes, w->scales, NULL);

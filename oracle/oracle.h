@@ -148,6 +148,8 @@ float *orc_llama_weight(orc_llama *model, int role, uint32_t layer);
 /* Random-init N(0, std) for matrices and N(1, 0.1) norms; quantizes matrices
  * when the config asks for it and keeps the dequantized copy for matmul. */
 void orc_llama_init_random(orc_llama *model, uint64_t seed, float std);
+/* The weight as drawn, before quantization (what a model file would hold). */
+const float *orc_llama_weight_source(const orc_llama *model, int role, uint32_t layer);
 /* Quantized payload of one matrix role (codes row-major, scales [n, groups]). */
 const uint8_t *orc_llama_codes(const orc_llama *model, int role, uint32_t layer);
 const float *orc_llama_scales(const orc_llama *model, int role, uint32_t layer);

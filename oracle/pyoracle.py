@@ -89,6 +89,8 @@ def lib():
         _lib.orc_llama_weight_len.argtypes = [C.c_void_p, C.c_int, C.c_uint32]
         _lib.orc_llama_weight.restype = C.POINTER(C.c_float)
         _lib.orc_llama_weight.argtypes = [C.c_void_p, C.c_int, C.c_uint32]
+        _lib.orc_llama_weight_source.restype = C.POINTER(C.c_float)
+        _lib.orc_llama_weight_source.argtypes = [C.c_void_p, C.c_int, C.c_uint32]
         _lib.orc_llama_codes.restype = C.POINTER(C.c_uint8)
         _lib.orc_llama_codes.argtypes = [C.c_void_p, C.c_int, C.c_uint32]
         _lib.orc_llama_scales.restype = C.POINTER(C.c_float)
@@ -373,6 +375,12 @@ class Llama:
         r = ROLES.index(role)
         n = lib().orc_llama_weight_len(self._p, r, layer)
         return np.ctypeslib.as_array(lib().orc_llama_weight(self._p, r, layer), (n,)).copy()
+
+    def weight_source(self, role, layer=0) -> np.ndarray:
+        """The weight before quantization (equal to weight() for dense roles)."""
+        r = ROLES.index(role)
+        n = lib().orc_llama_weight_len(self._p, r, layer)
+        return np.ctypeslib.as_array(lib().orc_llama_weight_source(self._p, r, layer), (n,)).copy()
 
     def codes(self, role, layer, nbytes) -> np.ndarray:
         r = ROLES.index(role)

@@ -15,13 +15,15 @@
 //  * Codes become exact small integers in f16 without a multiply: INT4 nibble
 //    pairs are masked into the mantissa of 1024.0 (one shift + one LOP3 per
 //    two codes, giving 1032 + code), INT8 bytes are placed under 0x64 with a
-//    byte permute (1152 + code). The bias term sum_k bias * x is removed per
-//    group with a per-column sum of the staged activations.
+//    byte permute (1152 + code); one packed f16 subtraction per two codes
+//    removes the bias exactly. (Folding the bias into a per-group correction
+//    instead would make the MMA accumulate values ~100x larger than the
+//    result and amplify its accumulation rounding by the same factor.)
 //  * Activations are split into f16 hi + lo (22 significant bits) after a
 //    per-CTA, per-column power-of-two prescale that keeps them in f16 range;
 //    hi and lo products accumulate into the same f32 accumulator.
-//  * Per group: acc -> (acc - bias * xsum) * scale[n, group], accumulated in
-//    f32 registers. Column prescales are undone exactly at the end.
+//  * Per group: acc * scale[n, group], accumulated in f32 registers. Column
+//    prescales are undone exactly at the end.
 //  * Split-K across CTAs when N alone cannot fill 148 SMs; partial sums go to
 //    the workspace and the last CTA of each row block (atomic ticket, no
 //    waiting) adds them in ascending split order, so results are
@@ -50,17 +52,21 @@ struct Fmt;
 template <>
 struct Fmt<0> {  // INT4: 32 codes per 16-byte lane chunk, 128 k per warp-step
     static constexpr int kStep = 128;
-    static constexpr float kBias = 1032.0f;
 };
 template <>
 struct Fmt<1> {  // INT8: 16 codes per chunk, 64 k per warp-step
     static constexpr int kStep = 64;
-    static constexpr float kBias = 1152.0f;
 };
 
 __device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;  // (a & b) ^ c
     asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
     return d;
 }
 
@@ -130,14 +136,12 @@ __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
     const int klen = min(p.slice_k, p.K - kb0);
     const int nsteps = klen / KSTEP;
     const int group_steps = p.group / KSTEP;
-    const int ngroups = klen / p.group;
     const int S = p.units_stride;
     const int Mc = p.M;  // real columns (<= 8 * NT)
 
     __half *xh = reinterpret_cast<__half *>(smem_raw);
     __half *xl = xh + (size_t)Mc * S * 8;
-    float *xsum = reinterpret_cast<float *>(xl + (size_t)Mc * S * 8);  // [Mc][ngroups]
-    float *unscale = xsum + (size_t)Mc * ngroups;                        // [Mc]
+    float *unscale = reinterpret_cast<float *>(xl + (size_t)Mc * S * 8);  // [Mc]
     __shared__ bool is_last;
 
     // ---- stage activations: warp w handles columns w, w + 8, ...
@@ -155,19 +159,13 @@ __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
         }
         const float up = ldexpf(1.0f, e);
         if (lane == 0) unscale[col] = ldexpf(1.0f, -e);
-        for (int gi = 0; gi < ngroups; gi++) {
-            float s = 0.f;
-            for (int k = gi * p.group + lane; k < (gi + 1) * p.group; k += 32) {
-                float v = xr[k] * up;
-                __half hi = __float2half_rn(v);
-                __half lo = __float2half_rn(v - __half2float(hi));
-                int slot = stage_slot<FMT>(k, S, col);
-                xh[slot] = hi;
-                xl[slot] = lo;
-                s += __half2float(hi) + __half2float(lo);
-            }
-            s = warp_sum(s);
-            if (lane == 0) xsum[col * ngroups + gi] = s;
+        for (int k = lane; k < klen; k += 32) {
+            float v = xr[k] * up;
+            __half hi = __float2half_rn(v);
+            __half lo = __float2half_rn(v - __half2float(hi));
+            int slot = stage_slot<FMT>(k, S, col);
+            xh[slot] = hi;
+            xl[slot] = lo;
         }
     }
     __syncthreads();
@@ -219,8 +217,10 @@ __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
                             uint32_t pa[4], pb[4];
 #pragma unroll
                             for (int i = 0; i < 4; i++) {
-                                pa[i] = lop3_and_xor(wa[q] >> (4 * i), 0x000F000Fu, 0x64086408u);
-                                pb[i] = lop3_and_xor(wb[q] >> (4 * i), 0x000F000Fu, 0x64086408u);
+                                pa[i] = hsub2(lop3_and_xor(wa[q] >> (4 * i), 0x000F000Fu, 0x64086408u),
+                                              0x64086408u);
+                                pb[i] = hsub2(lop3_and_xor(wb[q] >> (4 * i), 0x000F000Fu, 0x64086408u),
+                                              0x64086408u);
                             }
                             const int unit = ws * 16 + 4 * t + q;
                             const int phys = unit ^ ((unit >> 3) & 1);
@@ -246,10 +246,10 @@ __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
                             for (int h = 0; h < 2; h++) {
                                 const uint32_t xa = wa[2 * qq + h] ^ 0x80808080u;
                                 const uint32_t xb = wb[2 * qq + h] ^ 0x80808080u;
-                                lo_a[h] = prmt(xa, 0x64646464u, 0x4140u);
-                                hi_a[h] = prmt(xa, 0x64646464u, 0x4342u);
-                                lo_b[h] = prmt(xb, 0x64646464u, 0x4140u);
-                                hi_b[h] = prmt(xb, 0x64646464u, 0x4342u);
+                                lo_a[h] = hsub2(prmt(xa, 0x64646464u, 0x4140u), 0x64806480u);
+                                hi_a[h] = hsub2(prmt(xa, 0x64646464u, 0x4342u), 0x64806480u);
+                                lo_b[h] = hsub2(prmt(xb, 0x64646464u, 0x4140u), 0x64806480u);
+                                hi_b[h] = hsub2(prmt(xb, 0x64646464u, 0x4342u), 0x64806480u);
                             }
                             const int unit = ws * 8 + 2 * t + qq;
 #pragma unroll
@@ -267,20 +267,16 @@ __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
                             }
                         }
                     }
-                    // Group epilogue: remove the bias, apply the group scale.
+                    // Group epilogue: apply the group scale.
                     if ((ws + 1) % group_steps == 0) {
                         const int gi = ws / group_steps;
                         const float s0 = __ldg(sg + gi), s1 = __ldg(sg8 + gi);
 #pragma unroll
                         for (int jn = 0; jn < NT; jn++) {
-                            const int c0 = 2 * t + 8 * jn, c1 = c0 + 1;
-                            const float x0 = c0 < Mc ? xsum[c0 * ngroups + gi] : 0.f;
-                            const float x1 = c1 < Mc ? xsum[c1 * ngroups + gi] : 0.f;
-                            const float bias = Fmt<FMT>::kBias;
-                            res[jn][0] = fmaf(s0, fmaf(-bias, x0, acc[jn][0]), res[jn][0]);
-                            res[jn][1] = fmaf(s0, fmaf(-bias, x1, acc[jn][1]), res[jn][1]);
-                            res[jn][2] = fmaf(s1, fmaf(-bias, x0, acc[jn][2]), res[jn][2]);
-                            res[jn][3] = fmaf(s1, fmaf(-bias, x1, acc[jn][3]), res[jn][3]);
+                            res[jn][0] = fmaf(s0, acc[jn][0], res[jn][0]);
+                            res[jn][1] = fmaf(s0, acc[jn][1], res[jn][1]);
+                            res[jn][2] = fmaf(s1, acc[jn][2], res[jn][2]);
+                            res[jn][3] = fmaf(s1, acc[jn][3], res[jn][3]);
 #pragma unroll
                             for (int i = 0; i < 4; i++) acc[jn][i] = 0.f;
                         }
@@ -478,7 +474,7 @@ Plan make_plan(const QuantWeight &w, size_t m) {
         } else {
             if (S % 2 == 0) S++;
         }
-        return std::make_pair(S, (size_t)m * S * 16 * 2 + (size_t)m * gps * 4 + (size_t)m * 4);
+        return std::make_pair(S, (size_t)m * S * 16 * 2 + (size_t)m * 4);
     };
     while (groups_per_slice > 1 && smem_for(groups_per_slice).second > (size_t)kSmemBudget)
         groups_per_slice = (groups_per_slice + 1) / 2;

@@ -378,7 +378,10 @@ def _qmatmul_case(dev, fmt, m, k, n, group, seed, spot_rows=None):
 @pytest.mark.parametrize("m", [1, 4, 8, 16, 32, 33])
 @pytest.mark.parametrize("k,n", [(4096, 4096), (4096, 1024), (1024, 4096)])
 def test_quantized_matmul_g128(dev, fmt, m, k, n):
-    _qmatmul_case(dev, fmt, m, k, n, 128, seed=m * 31 + k + n)
+    err = _qmatmul_case(dev, fmt, m, k, n, 128, seed=m * 31 + k + n)
+    # Regression bound well inside the tolerance: outputs here are ~N(0, 1.3),
+    # an f32-class dot product of 4096 terms stays below 1e-4 absolute.
+    assert err < 1e-4, err
 
 
 @pytest.mark.parametrize("fmt", [orc.INT4, orc.INT8])
