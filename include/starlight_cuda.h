@@ -267,6 +267,38 @@ int slc_comm_unique_id(uint8_t out_id[128]);
 int slc_comm_init(slc_device *device, const uint8_t unique_id[128], int rank, int world);
 int slc_comm_world(const slc_device *device, int *rank, int *world);
 
+/* ---- EXTENSION (no counterpart in the reference): quantized matmul that
+ * allocates nothing ---------------------------------------------------------
+ * out[m, n] = x[m, k] . dequant(codes, scales)[n, k]^T, the computation of
+ * slc_dispatch(MatMulNT) on a GroupwiseQuantized weight, on device pointers
+ * the caller owns and a stream the caller names. For callers that cannot let
+ * a library allocate device memory: a host whose allocator or memory pool
+ * owns the GPU, a fixed memory budget, or a latency-critical loop in which
+ * cudaMalloc/cudaFree would synchronize the device. Such callers cannot create
+ * an slc_device (creation reserves a workspace).
+ *
+ * x: f32 [m, k]; codes: rows of ceil(k/2) bytes (INT4) or k bytes (INT8) in
+ * the slc_bind_quant format; scales: f32 [n, ceil(k/group_size)]; out: f32
+ * [m, n]; stream: a cudaStream_t (NULL = legacy default stream). The call is
+ * asynchronous on that stream.
+ *
+ * Scratch: the split-K partial sums and tickets live in one fixed device
+ * array of SLC_NOALLOC_SCRATCH_BYTES inside the library (on each device that
+ * uses it). The tickets must start at zero: each call clears them on the
+ * stream before its kernels. Problems whose scratch would exceed the array
+ * (decode-sized m <= 64 with large n * split factor) are rejected with
+ * SLC_ERR_OUT_OF_MEMORY and a message; m > 64 needs no scratch.
+ * The first call on each device (with that device current) looks up the
+ * array's device address; make that first call outside any stream capture.
+ * Calls that overlap in time on one device (several streams or host threads)
+ * share the array and race: serialize them, e.g. on one stream.
+ * Returns an slc_status; *error_message (if not NULL) is set to a static
+ * string on failure. */
+#define SLC_NOALLOC_SCRATCH_BYTES (8u << 20)
+int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes, const float *scales,
+                        uint64_t n, uint64_t k, uint32_t quant_format, uint32_t group_size,
+                        float *out, void *stream, const char **error_message);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif
