@@ -291,20 +291,49 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
     dev.synchronize()
     t1.synchronize()
     ms = t0.elapsed_time(t1)
-    total_bytes = 0
-    for ref, val in launches:
+
+    def algo_bytes(val):
         n, k = val.shape
-        total_bytes += n * k // 2 + 4 * n * (k // 128) + 4 * batch * (k + n)
+        return n * k // 2 + 4 * n * (k // 128) + 4 * batch * (k + n)
+
+    total_bytes = sum(algo_bytes(val) for _, val in launches)
     n_launch = len(launches)
     per_launch_bytes = total_bytes / n_launch
     per_launch_s = ms / 1e3 / (reps * n_launch)
     achieved = per_launch_bytes / per_launch_s / 1e9
+    # Per weight shape: every layer's matrix of one role in turn.
+    shapes = {}
+    for role in roles + ["lm_head"]:
+        subset = [lv for lv in launches if lv[1].shape == model.weight_ref(role, 0)[1].shape]
+        key = "x".join(str(d) for d in subset[0][1].shape)
+        if key in shapes:
+            continue
+
+        def run_subset():
+            for ref, val in subset:
+                n, k = val.shape
+                dev.dispatch(Op(OpCode.MatMulNT), [BufferRef(xbufs[k], 0, batch * k), ref],
+                             [Value.f32((batch, k)), val], [BufferRef(outs[n], 0, batch * n)],
+                             [Value.f32((batch, n))])
+        run_subset()
+        dev.synchronize()
+        with torch.cuda.stream(stream):
+            t0.record(stream)
+            for _ in range(reps):
+                run_subset()
+            t1.record(stream)
+        dev.synchronize()
+        t1.synchronize()
+        us = t0.elapsed_time(t1) * 1e3 / (reps * len(subset))
+        b = algo_bytes(subset[0][1])
+        shapes[key] = {"launch_us": round(us, 2), "gbs": round(b / us / 1e3, 1),
+                       "frac": round(b / us / 1e3 / peak[0], 3), "launches": len(subset)}
     traffic = profile_traffic()
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0], "traffic": traffic,
-            "kernel": "qgemv_mma<INT4> (MatMulNT, M=%d) over one decode step's weight mix" % batch,
+            "kernel": "qgemv_tma<INT4> (MatMulNT, M=%d) over one decode step's weight mix" % batch,
             "algorithmic_bytes_per_launch": per_launch_bytes, "launch_us": per_launch_s * 1e6,
-            "peak_source": peak[1]}
+            "peak_source": peak[1], "by_shape_NxK": shapes}
 
 
 def rmsnorm_gbs(dev, peak):
@@ -382,6 +411,9 @@ def run_ours(args, dist: Dist):
     dev.synchronize()
     device_ms = 0.0
     w0 = time.perf_counter()
+    # NVTX range (a no-op without a profiler) so a launch list can select the
+    # timed decode steps: ncu --nvtx --nvtx-include "decode/".
+    torch.cuda.nvtx.range_push("decode")
     for _ in range(args.steps):
         logits = model.step(DECODE, ids, np.full(B, past, np.uint32), 1, past)
         device_ms += model.last_step_ms()
@@ -389,6 +421,7 @@ def run_ours(args, dist: Dist):
         past += 1
     dev.synchronize()
     wall = time.perf_counter() - w0
+    torch.cuda.nvtx.range_pop()
     dist.barrier()
     launches = dev.launch_count() - launches0
     clocks = sampler.stop()

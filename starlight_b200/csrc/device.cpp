@@ -204,8 +204,9 @@ extern "C" int slc_device_create_ex(int ordinal, const slc_device_options *opt,
         cudaMalloc(&d->workspace, ws) != cudaSuccess ||
         cudaMemset(d->workspace, 0, ws) != cudaSuccess ||
         cudaMallocHost(&d->staging, stg) != cudaSuccess ||
-        cudaMalloc(&d->device_flag, sizeof(uint32_t)) != cudaSuccess ||
-        cudaMemset(d->device_flag, 0, sizeof(uint32_t)) != cudaSuccess) {
+        cudaHostAlloc(&d->host_flag, sizeof(uint32_t), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void **>(&d->device_flag), d->host_flag, 0) !=
+            cudaSuccess) {
         slc_device_destroy(d);
         return SLC_ERR_OUT_OF_MEMORY;
     }
@@ -224,7 +225,7 @@ extern "C" void slc_device_destroy(slc_device *d) {
     for (auto &b : d->buffers)
         if (b.alloc) cudaFree(b.alloc);
     if (d->workspace) cudaFree(d->workspace);
-    if (d->device_flag) cudaFree(d->device_flag);
+    if (d->host_flag) cudaFreeHost(d->host_flag);
     if (d->staging) cudaFreeHost(d->staging);
     if (d->stream) cudaStreamDestroy(d->stream);
     delete d;
@@ -387,6 +388,26 @@ extern "C" int slc_download_u32(slc_device *d, uint32_t buffer, uint32_t *out, u
     return download(d, buffer, out, len, true);
 }
 
+// Kernels record failures (a gather id out of range, a bounded wait that gave
+// up, a device-resident scalar out of bounds) in a mapped host word; the host
+// reads and clears it after every synchronization.
+static int check_device_flag(slc_device *d) {
+    volatile uint32_t *flag = d->host_flag;
+    const uint32_t code = *flag;
+    if (code == 0) return SLC_OK;
+    *flag = 0;
+    switch (code) {
+    case 1:
+        return exec_err(d, "id out of range");
+    case 2:
+        return exec_err(d, "a kernel's bounded wait timed out");
+    case 3:
+        return exec_err(d, "a device-resident scalar was out of bounds");
+    default:
+        return exec_err(d, "a kernel reported an error");
+    }
+}
+
 extern "C" int slc_synchronize(slc_device *d) {
     if (!d) return SLC_ERR_EXECUTION;
     int rc = flush_capture(d);
@@ -394,7 +415,7 @@ extern "C" int slc_synchronize(slc_device *d) {
     cudaSetDevice(d->ordinal);
     cudaError_t e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) return exec_err(d, "stream synchronization failed");
-    return SLC_OK;
+    return check_device_flag(d);
 }
 
 extern "C" int slc_copy_f32_from_device(slc_device *d, uint32_t buffer, uint64_t offset,

@@ -35,7 +35,8 @@ struct slc_device {
     uint64_t workspace_bytes = 0;
     char *staging = nullptr;
     uint64_t staging_bytes = 0;
-    uint32_t *device_flag = nullptr;
+    uint32_t *host_flag = nullptr;    // mapped pinned word: kernel error code (0 = none)
+    uint32_t *device_flag = nullptr;  // its device address
     slc_error last{};
     CaptureState *capture = nullptr;
     CommState *comm = nullptr;

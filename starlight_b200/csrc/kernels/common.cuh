@@ -47,6 +47,13 @@ __device__ __forceinline__ void st_stream_f4(float *p, float4 v) {
                  : "memory");
 }
 
+// L2-coherent load (skips L1): data written by other CTAs of the same launch.
+__device__ __forceinline__ float ld_cg_f32(const float *p) {
+    float v;
+    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+    return v;
+}
+
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
 }

@@ -35,6 +35,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "gemv_common.cuh"
 #include "kernels.h"
 
 namespace slc {
@@ -47,59 +48,6 @@ constexpr int kRowsPerCta = 16 * kWarps;
 constexpr int kPrefetch = 4;
 constexpr int kSmemBudget = 160 * 1024;
 
-template <int FMT>
-struct Fmt;
-template <>
-struct Fmt<0> {  // INT4: 32 codes per 16-byte lane chunk, 128 k per warp-step
-    static constexpr int kStep = 128;
-};
-template <>
-struct Fmt<1> {  // INT8: 16 codes per chunk, 64 k per warp-step
-    static constexpr int kStep = 64;
-};
-
-__device__ __forceinline__ uint32_t lop3_and_xor(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;  // (a & b) ^ c
-    asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t d;
-    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
-    return d;
-}
-
-__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
-                                         uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};"
-        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 lds128(const void *p) {
-    uint4 r;
-    uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "r"(a));
-    return r;
-}
-
-__device__ __forceinline__ float ld_cg(const float *p) {
-    float v;
-    asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
-    return v;
-}
-
 struct GemvArgs {
     const float *x;         // [M, K]
     const uint8_t *codes;   // [N, row_bytes]
@@ -111,19 +59,6 @@ struct GemvArgs {
     int units_stride;       // S: 16-byte units per smem row (padded)
     size_t row_bytes;
 };
-
-// Position of k (relative to the slice) inside the staged activation plane:
-// a 16-byte unit index (swizzled for conflict-free 128-bit reads) and the
-// f16 slot inside the unit (INT4 interleaves nibbles i and i+4).
-template <int FMT>
-__device__ __forceinline__ int stage_slot(int kr, int S, int col) {
-    int unit = kr >> 3, e = kr & 7;
-    if (FMT == 0) {
-        unit ^= (unit >> 3) & 1;
-        e = e < 4 ? 2 * e : 2 * (e - 4) + 1;
-    }
-    return (col * S + unit) * 8 + e;
-}
 
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
@@ -528,15 +463,29 @@ cudaError_t launch_fast(cudaStream_t s, const float *x, size_t m, const QuantWei
 // The first 64 Ki unsigned of the workspace are the split-K tickets (zeroed
 // once when the device is created and reset by every last CTA); the partial
 // sums follow.
-size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m) {
+namespace {
+size_t mma_workspace_bytes(const QuantWeight &w, size_t m) {
     Plan pl = make_plan(w, m);
     if (!pl.fast || pl.ksplit <= 1) return 0;
     if (pl.row_blocks > 64 * 1024) return (size_t)-1;
     return 64 * 1024 * sizeof(unsigned) + (size_t)pl.ksplit * m * w.n * sizeof(float);
 }
+}  // namespace
+
+size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m) {
+    if (m > 64) return 0;
+    size_t most = 0;
+    for (size_t m0 = 0; m0 < m; m0 += 32) {
+        const size_t mb = m - m0 < 32 ? m - m0 : 32;
+        size_t b = qgemv_tma_supported(w, mb) ? qgemv_tma_workspace_bytes(w, mb)
+                                              : mma_workspace_bytes(w, mb);
+        most = b > most ? b : most;
+    }
+    return most;
+}
 
 cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
-                    void *workspace, size_t workspace_bytes) {
+                    void *workspace, size_t workspace_bytes, uint32_t *err) {
     if (m == 0 || w.n == 0) return cudaSuccess;
     if (w.k == 0) return cudaMemsetAsync(out, 0, m * w.n * sizeof(float), s);
     // Prefill-sized inputs: one tiled GEMM pass over the weights.
@@ -546,8 +495,14 @@ cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight 
         size_t mb = m - m0 < 32 ? m - m0 : 32;
         const float *xb = x + m0 * w.k;
         float *ob = out + m0 * w.n;
+        if (qgemv_tma_supported(w, mb) && qgemv_tma_x_aligned(xb) &&
+            qgemv_tma_workspace_bytes(w, mb) <= workspace_bytes) {
+            cudaError_t e = qgemv_tma(s, xb, mb, w, ob, workspace, err);
+            if (e != cudaSuccess) return e;
+            continue;
+        }
         Plan pl = make_plan(w, mb);
-        size_t need = qmatmul_workspace_bytes(w, mb);
+        size_t need = mma_workspace_bytes(w, mb);
         if (pl.fast && need <= workspace_bytes) {
             cudaError_t e;
             if (w.format == 0) {

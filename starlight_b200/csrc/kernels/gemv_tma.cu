@@ -1,0 +1,628 @@
+// Decode GEMV for group-quantized weights, fed by bulk asynchronous copies
+// (TMA) into a shared-memory ring: out[m, n] = sum_k x[m, k] * w[n, k] with
+// w = code * scale[n, k / group], small M (decode batch).
+//
+// Parity target: dequantize, then backend-cpu's f32 matmul_nt
+// (crates/backends/backend-cpu/src/reference/matmul.rs:29-59).
+//
+// HBM-bound on the payload; algorithmic bytes per launch
+//   N * row_bytes + 4 * N * K / group + 4 * M * (K + N).
+//
+// Work decomposition. The weight matrix is cut into tiles of 16 rows (one
+// mma.sync M tile) and every tile into warp-steps of 64 bytes per row (128
+// INT4 or 64 INT8 codes, always inside one quantization group). The
+// n_tiles * steps_per_row warp-steps are ordered tile-major and split into
+// one contiguous, balanced range per CTA (persistent grid, one CTA per SM),
+// so every CTA streams the same number of bytes to within one warp-step.
+//
+// Per CTA, warp 8 is the producer: it cuts its range into stages of at most
+// 32 warp-steps (16 rows x <= 2 KiB) that never cross a tile, and copies
+// each row of a stage with one cp.async.bulk into a ring slot (row pitch
+// 2 KiB + 64 B, so that the consumers' 16-byte reads of two rows per phase
+// are conflict-free), completing on the slot's "full" mbarrier. Bulk copies
+// are issued per row of up to 2 KiB because their throughput is bounded by
+// the copy count (measured on B200: 256 B copies reach 1.3 TB/s, >= 2 KiB
+// copies the full HBM rate).
+//
+// Warps 0..7 consume: warp w takes warp-steps w, w + 8, ... of the stage;
+// each lane reads 16-byte chunks of rows g and g + 8, turns codes into exact
+// f16 integers (magic-number LOP3 / byte permute + one packed subtraction)
+// and multiplies them with the activations on the tensor cores (mma.sync
+// m16n8k16, f16 x f16 -> f32), activations split into f16 hi + lo after a
+// power-of-two prescale per column; the group scale is applied after every
+// warp-step. Each warp releases the slot on its "empty" mbarrier. All waits
+// are bounded (1 s), after which the kernel records an error for the host
+// and skips the rest of its work.
+//
+// Activations are staged once per CTA (all of K, the permuted f16 layout of
+// gemv_common.cuh); shapes whose activations do not fit next to the ring
+// use the register-streaming kernel of gemv_quant.cu.
+//
+// Results: at the end of a tile's run the 8 warps' sums are added in warp
+// order through shared memory. A CTA that covered the whole tile writes the
+// output; otherwise each contributing CTA writes a partial to a workspace
+// slot (its rank among the tile's contributors) and the last one to arrive
+// (atomic ticket, no waiting) adds the slots in ascending order, so results
+// are deterministic for a given shape.
+#include <math.h>
+
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "gemv_common.cuh"
+#include "kernels.h"
+#include "tensormap.h"
+#include "tma.cuh"
+
+namespace slc {
+namespace k {
+namespace {
+
+constexpr int kTiles = 8;                         // 16-row tiles per block
+constexpr int kTileRows = 16;                     // rows per tile (mma M)
+constexpr int kBlockRows = kTileRows * kTiles;    // 128 rows per block
+constexpr int kStepBytes = 64;                    // bytes per row per warp-step
+constexpr int kRun = 5;                           // warp-steps per stage
+constexpr int kPitch = kRun * kStepBytes;         // 320 bytes: = 64 mod 128, so the 16-byte
+                                                  // reads of rows g and g + 1 never collide
+constexpr int kScaleBox = 8;                      // scale groups per row per stage (box)
+constexpr int kCodeBytes = kBlockRows * kPitch;   // 40 KiB
+constexpr int kScaleBytes = kBlockRows * kScaleBox * 4;
+constexpr int kSlotBytes = kCodeBytes + kScaleBytes;  // 44 KiB
+constexpr int kMaxStages = 5;
+constexpr int kMinStages = 3;
+constexpr int kSmemLimit = 227 * 1024;
+
+struct TmaArgs {
+    CUtensorMap codes_map;  // [N][row_bytes / 8] u64, box [128][32]
+    CUtensorMap scales_map; // [N][groups] f32, box [128][8]
+    const float *x;         // [M, K]
+    const uint8_t *codes;   // [N, row_bytes]
+    const float *scales;    // [N, groups]
+    float *out;             // [M, N]
+    float *partials;        // [slots, M, N]
+    unsigned *tickets;      // [n_blocks]
+    uint32_t *err;          // device error word or null
+    int M, N, K, groups;
+    int gs_shift;           // log2(warp-steps per quantization group)
+    long long row_bytes;
+    long long spr;          // warp-steps per row
+    long long total;        // n_blocks * spr
+    int nstage;
+    int S;                  // 16-byte units per staged activation column (padded)
+    int ring_bytes;         // shared offset of the activation planes
+    int unscale_floats;     // M * spr rounded up to an even count
+};
+
+template <int CW>
+__device__ __forceinline__ void consumer_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
+}
+
+// CTA whose range contains unit u (ranges are [c * total / grid, ...)).
+__device__ __forceinline__ long long owner(long long u, long long total, long long grid) {
+    return ((u + 1) * grid - 1) / total;
+}
+
+__device__ __forceinline__ int prescale_exponent(float mx) {
+    int e = 0;
+    if (mx > 0.f) {
+        int ex;
+        frexpf(mx, &ex);
+        e = 14 - ex;
+        e = e > 126 ? 126 : (e < -126 ? -126 : e);
+    }
+    return e;
+}
+
+// Position of activation k of column col in the f16 planes. INT4: lane quad
+// t of a warp-step reads codes 32t .. 32t + 31 as four words q of eight
+// codes, so the 8-value unit (ws, q, t) sits at ws * 16 + 4q + t: the four
+// quads read consecutive 16-byte units (conflict-free), and within a unit
+// value e sits at the f16 slot of the nibble pair (i, i + 4) that int4_pairs
+// produces. INT8: natural order (lane quads read units 2t, 2t + 1).
+template <int FMT>
+__device__ __forceinline__ int tma_slot(int kr, int S, int col) {
+    if (FMT == 0) {
+        const int unit = (kr >> 7) * 16 + ((kr >> 3) & 3) * 4 + ((kr >> 5) & 3);
+        const int e = kr & 7;
+        return (col * S + unit) * 8 + (e < 4 ? 2 * e : 2 * (e - 4) + 1);
+    }
+    return (col * S + (kr >> 3)) * 8 + (kr & 7);
+}
+
+// Stages all of x into the permuted f16 hi/lo planes (consumer warps only).
+// Every block of one warp-step's k values (128 for INT4, 64 for INT8) of a
+// column gets its own power-of-two prescale, computed by one warp from one
+// vectorised load per lane, so staging needs no CTA-wide reduction; the
+// inverse (`unscale[col][step]`) is applied after the step's MMAs.
+template <int FMT, int CW>
+__device__ void stage_x(const TmaArgs &p, __half *xh, __half *xl, float *unscale) {
+    constexpr int KSTEP = Fmt<FMT>::kStep;
+    constexpr int PER = KSTEP / 32;  // values per lane: 4 (INT4) or 2 (INT8)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int spr = (int)p.spr;
+    const int blocks = p.M * spr;
+    for (int b = warp; b < blocks; b += CW) {
+        const int col = b / spr, st = b - col * spr;
+        const int k0 = st * KSTEP + lane * PER;
+        const float *src = p.x + (long long)col * p.K + k0;
+        float v[PER];
+        if constexpr (PER == 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(src));
+            v[0] = q.x;
+            v[1] = q.y;
+            v[2] = q.z;
+            v[3] = q.w;
+        } else {
+            const float2 q = __ldg(reinterpret_cast<const float2 *>(src));
+            v[0] = q.x;
+            v[1] = q.y;
+        }
+        float mx = 0.f;
+#pragma unroll
+        for (int i = 0; i < PER; i++) mx = fmaxf(mx, fabsf(v[i]));
+        const int e = prescale_exponent(warp_max(mx));
+        const float up = ldexpf(1.0f, e);
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const float y = v[i] * up;
+            const __half hi = __float2half_rn(y);
+            const __half lo = __float2half_rn(y - __half2float(hi));
+            const int slot = tma_slot<FMT>(k0 + i, p.S, col);
+            xh[slot] = hi;
+            xl[slot] = lo;
+        }
+        if (lane == 0) unscale[b] = ldexpf(1.0f, -e);
+    }
+    consumer_sync<CW>();
+}
+
+// One warp-step (64 bytes of rows g and g + 8 per lane quad) into acc. The
+// MMAs go to four independent accumulator chains (hi / lo activation part x
+// even / odd chunk) that are added at the end, so that consecutive MMAs do
+// not wait on each other's results.
+template <int FMT, int NT>
+__device__ __forceinline__ void warp_step(const unsigned char *tile, int pitch, int ws,
+                                          const __half *xh, const __half *xl, int S, int Mc,
+                                          int g, int t, float (&acc)[NT][4]) {
+    float ch[4][NT][4];
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+#pragma unroll
+        for (int jn = 0; jn < NT; jn++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) ch[c][jn][i] = 0.f;
+    const uint4 wg = lds128(tile);
+    const uint4 wg8 = lds128(tile + 8 * pitch);
+    const uint32_t wa[4] = {wg.x, wg.y, wg.z, wg.w};
+    const uint32_t wb[4] = {wg8.x, wg8.y, wg8.z, wg8.w};
+    if (FMT == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            uint32_t pa[4], pb[4];
+            int4_pairs(wa[q], pa);
+            int4_pairs(wb[q], pb);
+            const int phys = ws * 16 + 4 * q + t;
+            const int c = (q & 1) * 2;
+#pragma unroll
+            for (int jn = 0; jn < NT; jn++) {
+                const int col = g + 8 * jn;
+                uint4 bh = make_uint4(0, 0, 0, 0), bl = bh;
+                if (col < Mc) {
+                    bh = lds128(xh + ((size_t)col * S + phys) * 8);
+                    bl = lds128(xl + ((size_t)col * S + phys) * 8);
+                }
+                mma16816(ch[c][jn], pa[0], pb[0], pa[1], pb[1], bh.x, bh.y);
+                mma16816(ch[c + 1][jn], pa[0], pb[0], pa[1], pb[1], bl.x, bl.y);
+                mma16816(ch[c][jn], pa[2], pb[2], pa[3], pb[3], bh.z, bh.w);
+                mma16816(ch[c + 1][jn], pa[2], pb[2], pa[3], pb[3], bl.z, bl.w);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int qq = 0; qq < 2; qq++) {
+            uint32_t lo_a[2], hi_a[2], lo_b[2], hi_b[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t xa = wa[2 * qq + h] ^ 0x80808080u;
+                const uint32_t xb = wb[2 * qq + h] ^ 0x80808080u;
+                lo_a[h] = hsub2(prmt(xa, 0x64646464u, 0x4140u), 0x64806480u);
+                hi_a[h] = hsub2(prmt(xa, 0x64646464u, 0x4342u), 0x64806480u);
+                lo_b[h] = hsub2(prmt(xb, 0x64646464u, 0x4140u), 0x64806480u);
+                hi_b[h] = hsub2(prmt(xb, 0x64646464u, 0x4342u), 0x64806480u);
+            }
+            const int unit = ws * 8 + 2 * t + qq;
+#pragma unroll
+            for (int jn = 0; jn < NT; jn++) {
+                const int col = g + 8 * jn;
+                uint4 bh = make_uint4(0, 0, 0, 0), bl = bh;
+                if (col < Mc) {
+                    bh = lds128(xh + ((size_t)col * S + unit) * 8);
+                    bl = lds128(xl + ((size_t)col * S + unit) * 8);
+                }
+                mma16816(ch[0][jn], lo_a[0], lo_b[0], hi_a[0], hi_b[0], bh.x, bh.y);
+                mma16816(ch[1][jn], lo_a[0], lo_b[0], hi_a[0], hi_b[0], bl.x, bl.y);
+                mma16816(ch[2][jn], lo_a[1], lo_b[1], hi_a[1], hi_b[1], bh.z, bh.w);
+                mma16816(ch[3][jn], lo_a[1], lo_b[1], hi_a[1], hi_b[1], bl.z, bl.w);
+            }
+        }
+    }
+#pragma unroll
+    for (int jn = 0; jn < NT; jn++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[jn][i] = (ch[0][jn][i] + ch[2][jn][i]) + (ch[1][jn][i] + ch[3][jn][i]);
+}
+
+// The warp-steps j = h, h + SPLIT, ... of a stage for one warp (tile rows at
+// `base`), scaled into res. FULL: the stage holds all kRun steps (no guards,
+// so the compiler can interleave the steps).
+template <int FMT, int NT, int SPLIT, bool FULL>
+__device__ __forceinline__ void stage_math(const TmaArgs &p, const unsigned char *base,
+                                           const float *ssl, int step0, int run, int h,
+                                           const __half *xh, const __half *xl,
+                                           const float *unscale, int g, int t,
+                                           float (&res)[NT][4]) {
+    const int g4 = (step0 >> p.gs_shift) & ~3;
+    const int Mc = p.M;
+#pragma unroll
+    for (int jj = 0; jj < (kRun + SPLIT - 1) / SPLIT; jj++) {
+        const int j = jj * SPLIT + h;
+        if (j < kRun && (FULL || j < run)) {
+            float acc[NT][4];
+            const int sw = step0 + j;
+            warp_step<FMT, NT>(base + j * kStepBytes, kPitch, sw, xh, xl, p.S, Mc, g, t, acc);
+            const int gi = (sw >> p.gs_shift) - g4;
+            const float s0 = ssl[gi], s1 = ssl[8 * kScaleBox + gi];
+#pragma unroll
+            for (int jn = 0; jn < NT; jn++) {
+                const int c0 = 2 * t + 8 * jn, c1 = c0 + 1;
+                const float u0s = c0 < Mc ? unscale[c0 * (int)p.spr + sw] : 0.f;
+                const float u1s = c1 < Mc ? unscale[c1 * (int)p.spr + sw] : 0.f;
+                res[jn][0] = fmaf(s0 * u0s, acc[jn][0], res[jn][0]);
+                res[jn][1] = fmaf(s0 * u1s, acc[jn][1], res[jn][1]);
+                res[jn][2] = fmaf(s1 * u0s, acc[jn][2], res[jn][2]);
+                res[jn][3] = fmaf(s1 * u1s, acc[jn][3], res[jn][3]);
+            }
+        }
+    }
+}
+
+// SPLIT consumer warps share each 16-row tile (warp w: tile w % 8, steps
+// h = w / 8, h + SPLIT, ... of every stage); their sums meet in shared
+// memory at the end of a block's run.
+template <int FMT, int NT, int SPLIT>
+__global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
+    qgemv_tma(const __grid_constant__ TmaArgs p) {
+    constexpr int CW = kTiles * SPLIT;  // consumer warps
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int tile = warp % kTiles, h = warp / kTiles;
+    const int Mc = p.M;
+
+    unsigned char *ring = smem;
+    __half *xh = reinterpret_cast<__half *>(smem + p.ring_bytes);
+    __half *xl = xh + (size_t)Mc * p.S * 8;
+    float *unscale = reinterpret_cast<float *>(xl + (size_t)Mc * p.S * 8);  // [M][spr]
+    float *red = unscale + p.unscale_floats;  // [kTiles][32 lanes][16] (SPLIT > 1)
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + (SPLIT > 1 ? kTiles * 32 * 16 : 0));
+    uint64_t *empty = full + kMaxStages;
+    int *last_flag = reinterpret_cast<int *>(empty + kMaxStages);
+    volatile int *abort = last_flag + 1;  // set when a wait timed out
+
+    const long long grid = gridDim.x, cta = blockIdx.x;
+    const long long u0 = cta * p.total / grid, u1 = (cta + 1) * p.total / grid;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nstage; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], CW);
+        }
+        fence_mbar_init();
+        *abort = 0;
+    }
+    __syncthreads();
+
+    if (warp == CW) {
+        // ---- producer: per stage one box of codes (128 rows x 256 bytes from
+        // warp-step step0) and one box of scales (128 rows x groups g4 ..
+        // g4 + 7, g4 rounded down to 4 groups = 16 bytes).
+        if (lane == 0) {
+            prefetch_tensormap(&p.codes_map);
+            prefetch_tensormap(&p.scales_map);
+            const uint64_t pol = policy_evict_first();
+            int slot = 0, phase = 0;
+            bool first_pass = true;
+            for (long long u = u0; u < u1;) {
+                const long long blk = u / p.spr;
+                const long long run_end = min(u1, (blk + 1) * p.spr);
+                while (u < run_end) {
+                    const int run = (int)min((long long)kRun, run_end - u);
+                    if (!first_pass && !mbar_wait(&empty[slot], phase ^ 1, p.err, abort)) return;
+                    const long long step0 = u - blk * p.spr;
+                    const int g4 = (int)(step0 >> p.gs_shift) & ~3;
+                    unsigned char *sl = ring + slot * kSlotBytes;
+                    mbar_arrive_expect_tx(&full[slot], (uint32_t)kSlotBytes);
+                    tma_load_2d(sl, &p.codes_map, (int)(step0 * (kStepBytes / 8)),
+                                (int)(blk * kBlockRows), &full[slot], pol);
+                    tma_load_2d(sl + kCodeBytes, &p.scales_map, g4, (int)(blk * kBlockRows),
+                                &full[slot], pol);
+                    u += run;
+                    if (++slot == p.nstage) {
+                        slot = 0;
+                        phase ^= 1;
+                        first_pass = false;
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ---- consumers.
+    stage_x<FMT, CW>(p, xh, xl, unscale);
+    float res[NT][4];
+    int slot = 0, phase = 0;
+    for (long long u = u0; u < u1;) {
+        const long long blk = u / p.spr;
+        const long long run_end = min(u1, (blk + 1) * p.spr);
+        const int row0 = (int)blk * kBlockRows + tile * kTileRows;
+        const bool active = row0 < p.N;
+#pragma unroll
+        for (int jn = 0; jn < NT; jn++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) res[jn][i] = 0.f;
+        while (u < run_end) {
+            const int run = (int)min((long long)kRun, run_end - u);
+            const int step0 = (int)(u - blk * p.spr);  // warp-step index within the row
+            // After a timed-out wait the CTA keeps its control flow (every
+            // named barrier is still reached) but skips waits and math.
+            const bool ready = !*abort && mbar_wait(&full[slot], phase, p.err, abort);
+            if (ready && active) {
+                const unsigned char *sl = ring + slot * kSlotBytes;
+                const unsigned char *base = sl + (tile * kTileRows + g) * kPitch + t * 16;
+                const float *ssl = reinterpret_cast<const float *>(sl + kCodeBytes) +
+                                   (tile * kTileRows + g) * kScaleBox;
+                if (run == kRun)
+                    stage_math<FMT, NT, SPLIT, true>(p, base, ssl, step0, run, h, xh, xl, unscale,
+                                                     g, t, res);
+                else
+                    stage_math<FMT, NT, SPLIT, false>(p, base, ssl, step0, run, h, xh, xl,
+                                                      unscale, g, t, res);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            u += run;
+            if (++slot == p.nstage) {
+                slot = 0;
+                phase ^= 1;
+            }
+        }
+
+        // ---- end of this CTA's run over the block.
+        if (SPLIT > 1) {
+            // Warps h > 0 hand their sums to warp h = 0 of the same tile.
+            float *rl = red + (tile * 32 + lane) * 16;
+            if (h > 0) {
+#pragma unroll
+                for (int jn = 0; jn < NT; jn++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) rl[jn * 4 + i] = res[jn][i];
+            }
+            consumer_sync<CW>();
+            if (h == 0) {
+#pragma unroll
+                for (int jn = 0; jn < NT; jn++)
+#pragma unroll
+                    for (int i = 0; i < 4; i++) res[jn][i] += rl[jn * 4 + i];
+            }
+            consumer_sync<CW>();
+        }
+        const long long first = owner(blk * p.spr, p.total, grid);
+        const long long last = owner((blk + 1) * p.spr - 1, p.total, grid);
+        const int count = (int)(last - first + 1);
+        float *dst = count == 1 ? p.out : p.partials + (cta - first) * (long long)Mc * p.N;
+        if (active && h == 0) {
+#pragma unroll
+            for (int jn = 0; jn < NT; jn++) {
+                const int c0 = 2 * t + 8 * jn, c1 = c0 + 1;
+                if (c0 < Mc) {
+                    dst[(size_t)c0 * p.N + row0 + g] = res[jn][0];
+                    dst[(size_t)c0 * p.N + row0 + g + 8] = res[jn][2];
+                }
+                if (c1 < Mc) {
+                    dst[(size_t)c1 * p.N + row0 + g] = res[jn][1];
+                    dst[(size_t)c1 * p.N + row0 + g + 8] = res[jn][3];
+                }
+            }
+        }
+        if (count > 1) {
+            __threadfence();
+            consumer_sync<CW>();
+            if (threadIdx.x == 0) {
+                const unsigned ticket = atomicAdd(&p.tickets[blk], 1u);
+                *last_flag = ticket == (unsigned)(count - 1);
+            }
+            consumer_sync<CW>();
+            const bool is_last = *last_flag;
+            consumer_sync<CW>();  // last_flag is rewritten by the next shared block
+            if (is_last) {
+                __threadfence();
+                const int rows_here = min(kBlockRows, p.N - (int)blk * kBlockRows);
+                for (int i = threadIdx.x; i < Mc * rows_here; i += CW * 32) {
+                    const int c = i / rows_here, r = (int)blk * kBlockRows + i % rows_here;
+                    float v = 0.f;
+                    for (int sl = 0; sl < count; sl++)
+                        v += ld_cg_f32(p.partials + ((long long)sl * Mc + c) * p.N + r);
+                    p.out[(size_t)c * p.N + r] = v;
+                }
+                if (threadIdx.x == 0) p.tickets[blk] = 0u;  // ready for the next launch
+            }
+        }
+    }
+}
+
+struct TmaPlan {
+    bool ok = false;
+    int nstage = 0, S = 0, ring_bytes = 0, grid = 0, slots = 0, unscale_floats = 0;
+    long long spr = 0, total = 0;
+    size_t smem = 0;
+};
+
+int padded_stride(int fmt, long long units) {
+    long long S = units;
+    if (fmt == 0) {
+        while (S % 8 != 4) S++;
+    } else if (S % 2 == 0) {
+        S++;
+    }
+    return (int)S;
+}
+
+TmaPlan make_tma_plan(const QuantWeight &w, size_t m) {
+    TmaPlan pl;
+    const int kstep = w.format == 0 ? Fmt<0>::kStep : Fmt<1>::kStep;
+    if (m < 1 || m > 32 || w.n % kTileRows != 0 || w.k % w.group != 0 || w.group % kstep != 0 ||
+        w.row_bytes % kStepBytes != 0 || !aligned16(w.codes) || !aligned16(w.scales) ||
+        w.groups % 4 != 0 || w.n > (1u << 24) || w.k > (1u << 24) || w.k == 0)
+        return pl;
+    const size_t gsteps = w.group / kstep;
+    if ((gsteps & (gsteps - 1)) != 0) return pl;  // power of two: shifts in the hot loop
+    pl.spr = (long long)(w.row_bytes / kStepBytes);
+    const long long n_blocks = (long long)((w.n + kBlockRows - 1) / kBlockRows);
+    if (n_blocks > 64 * 1024) return pl;
+    pl.total = n_blocks * pl.spr;
+    pl.grid = (int)std::min<long long>(pl.total, kSmCount);
+    pl.S = padded_stride(w.format, (long long)w.k / 8);
+    const size_t xbytes = (size_t)m * pl.S * 16 * 2;
+    pl.unscale_floats = (int)(((long long)m * pl.spr + 1) / 2 * 2);
+    const size_t fixed = (size_t)pl.unscale_floats * 4 + (size_t)kTiles * 32 * 16 * 4 +
+                         2 * kMaxStages * 8 + 16;  // unscale, split sums, barriers, flags
+    for (pl.nstage = kMaxStages; pl.nstage >= kMinStages; pl.nstage--) {
+        pl.ring_bytes = pl.nstage * kSlotBytes;
+        pl.smem = pl.ring_bytes + xbytes + fixed;
+        if (pl.smem <= (size_t)kSmemLimit) break;
+    }
+    if (pl.nstage < kMinStages) return pl;
+    // Partial slots: the most CTAs that share one block (each CTA covers
+    // spr * n_blocks / grid warp-steps).
+    pl.slots = (int)std::min<long long>(pl.grid, (pl.grid + n_blocks - 1) / n_blocks + 1);
+    pl.ok = true;
+    return pl;
+}
+
+// Tensor maps of a weight, encoded once and cached by everything they encode.
+struct MapKey {
+    const void *codes, *scales;
+    size_t n, row_bytes, groups;
+    bool operator==(const MapKey &o) const {
+        return codes == o.codes && scales == o.scales && n == o.n && row_bytes == o.row_bytes &&
+               groups == o.groups;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey &k) const {
+        size_t h = std::hash<const void *>()(k.codes) * 31 + std::hash<const void *>()(k.scales);
+        return h * 131 + k.n * 7 + k.row_bytes * 3 + k.groups;
+    }
+};
+struct MapPair {
+    CUtensorMap codes, scales;
+};
+
+bool tensor_maps(const QuantWeight &w, MapPair *out) {
+    static std::mutex mu;
+    static std::unordered_map<MapKey, MapPair, MapKeyHash> cache;
+    const MapKey key{w.codes, w.scales, w.n, w.row_bytes, w.groups};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *out = it->second;
+        return true;
+    }
+    MapPair mp;
+    if (!encode_tensor_map_2d(&mp.codes, CU_TENSOR_MAP_DATA_TYPE_UINT64, w.codes, w.row_bytes / 8,
+                              w.n, w.row_bytes, kPitch / 8, kBlockRows) ||
+        !encode_tensor_map_2d(&mp.scales, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales, w.groups, w.n,
+                              w.groups * 4, kScaleBox, kBlockRows))
+        return false;
+    if (cache.size() > 8192) cache.clear();
+    cache.emplace(key, mp);
+    *out = mp;
+    return true;
+}
+
+template <int FMT, int NT, int SPLIT>
+cudaError_t launch_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                       const TmaPlan &pl, void *ws, uint32_t *err) {
+    TmaArgs a{};
+    MapPair maps;
+    if (!tensor_maps(w, &maps)) return cudaErrorInvalidValue;
+    a.codes_map = maps.codes;
+    a.scales_map = maps.scales;
+    a.x = x;
+    a.codes = w.codes;
+    a.scales = w.scales;
+    a.out = out;
+    a.M = (int)m;
+    a.N = (int)w.n;
+    a.K = (int)w.k;
+    a.groups = (int)w.groups;
+    a.gs_shift = 0;
+    while ((1u << a.gs_shift) < w.group / Fmt<FMT>::kStep) a.gs_shift++;
+    a.row_bytes = (long long)w.row_bytes;
+    a.spr = pl.spr;
+    a.total = pl.total;
+    a.nstage = pl.nstage;
+    a.S = pl.S;
+    a.ring_bytes = pl.ring_bytes;
+    a.unscale_floats = pl.unscale_floats;
+    a.err = err;
+    a.tickets = static_cast<unsigned *>(ws);
+    a.partials = reinterpret_cast<float *>(static_cast<char *>(ws) + 64 * 1024 * sizeof(unsigned));
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(qgemv_tma<FMT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemLimit);
+        configured = true;
+    }
+    qgemv_tma<FMT, NT, SPLIT><<<pl.grid, (kTiles * SPLIT + 1) * 32, pl.smem, s>>>(a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t qgemv_tma_workspace_bytes(const QuantWeight &w, size_t m) {
+    TmaPlan pl = make_tma_plan(w, m);
+    if (!pl.ok) return (size_t)-1;
+    return 64 * 1024 * sizeof(unsigned) + (pl.slots > 1 ? (size_t)pl.slots * m * w.n * 4 : 0);
+}
+
+bool qgemv_tma_supported(const QuantWeight &w, size_t m) { return make_tma_plan(w, m).ok; }
+
+bool qgemv_tma_x_aligned(const float *x) { return aligned16(x); }
+
+cudaError_t qgemv_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                      void *workspace, uint32_t *err) {
+    TmaPlan pl = make_tma_plan(w, m);
+    if (!pl.ok || !aligned16(x)) return cudaErrorInvalidValue;
+    const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
+    // One column tile: two warps per 16-row tile (17 warps, 96 registers
+    // each, no spills); more columns need the registers of one warp per tile.
+    if (w.format == 0)
+        return nt == 1 ? launch_tma<0, 1, 2>(s, x, m, w, out, pl, workspace, err)
+             : nt == 2 ? launch_tma<0, 2, 1>(s, x, m, w, out, pl, workspace, err)
+                       : launch_tma<0, 4, 1>(s, x, m, w, out, pl, workspace, err);
+    return nt == 1 ? launch_tma<1, 1, 2>(s, x, m, w, out, pl, workspace, err)
+         : nt == 2 ? launch_tma<1, 2, 1>(s, x, m, w, out, pl, workspace, err)
+                   : launch_tma<1, 4, 1>(s, x, m, w, out, pl, workspace, err);
+}
+
+}  // namespace k
+}  // namespace slc

@@ -78,9 +78,16 @@ struct QuantWeight {
 // Tiled SIMT GEMM with the weight dequantized on load (prefill-sized m).
 cudaError_t qgemm_f32(cudaStream_t s, const float *a, size_t m, const QuantWeight &w, float *out);
 size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m);
-// out[m, n] = x[m, k] . dequant(w)[n, k]^T
+// out[m, n] = x[m, k] . dequant(w)[n, k]^T. `err` (optional) receives the
+// error code of a kernel whose bounded wait gave up.
 cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
-                    void *workspace, size_t workspace_bytes);
+                    void *workspace, size_t workspace_bytes, uint32_t *err = nullptr);
+// TMA-fed decode GEMV (gemv_tma.cu), small m; x must be 16-byte aligned.
+bool qgemv_tma_supported(const QuantWeight &w, size_t m);
+bool qgemv_tma_x_aligned(const float *x);
+size_t qgemv_tma_workspace_bytes(const QuantWeight &w, size_t m);
+cudaError_t qgemv_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                      void *workspace, uint32_t *err);
 cudaError_t quantize(cudaStream_t s, const float *w, size_t n, size_t k, size_t group,
                      int format, uint8_t *codes, float *scales);
 cudaError_t dequantize(cudaStream_t s, const QuantWeight &w, float *out);

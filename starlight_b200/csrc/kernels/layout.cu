@@ -7,6 +7,7 @@
 // a multiple of 4 and the pointers are 16-byte aligned.
 #include "common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 namespace slc {
 namespace k {
@@ -27,7 +28,7 @@ __device__ __forceinline__ bool source_row(const RowMap &m, size_t r, size_t *sr
     case kGather: {
         uint32_t id = m.ids[r];
         if ((size_t)id >= m.vocab) {  // host validated already; guard anyway
-            if (m.error_flag) atomicOr(m.error_flag, 1u);
+            report_error(m.error_flag, kErrGatherId);
             return false;
         }
         *src = id;

@@ -1,0 +1,19 @@
+// Host-side encoding of TMA tensor maps (driver entry point resolved once
+// through the runtime, so the library does not link libcuda directly).
+#pragma once
+
+#include <cuda.h>
+#include <stdint.h>
+
+namespace slc {
+namespace k {
+
+// A 2-D row-major tensor [rows][inner] of `dtype`, rows `row_stride_bytes`
+// apart, copied in boxes of [box_rows][box_inner] without swizzle; elements
+// outside the tensor read as zero. Returns false when the driver refuses.
+bool encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                          uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                          uint32_t box_inner, uint32_t box_rows);
+
+}  // namespace k
+}  // namespace slc

@@ -248,7 +248,8 @@ bool weight_of(Checker &ck, uint64_t i, uint64_t rows, uint64_t kk, Weight *w) {
 cudaError_t matmul_rows(slc_device *d, const float *x, uint64_t rows, uint64_t kk,
                         const Weight &w, uint64_t n, float *y) {
     if (w.quant)
-        return k::qmatmul(d->stream, x, rows, w.q, y, gemv_workspace(d), gemv_workspace_bytes(d));
+        return k::qmatmul(d->stream, x, rows, w.q, y, gemv_workspace(d), gemv_workspace_bytes(d),
+                          d->device_flag);
     return k::matmul_f32(d->stream, x, w.dense, y, 1, 1, rows, kk, n, true);
 }
 
@@ -295,7 +296,7 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
             REQUIRE(weight_of(ck, 1, n, kk, &w));
             if (!launch || batch == 0) return SLC_OK;
             return finish(ck, k::qmatmul(s, a, batch * m, w.q, ck.output(), gemv_workspace(d),
-                                         gemv_workspace_bytes(d)));
+                                         gemv_workspace_bytes(d), d->device_flag));
         }
         const float *w = ck.f32(1);
         REQUIRE(w);

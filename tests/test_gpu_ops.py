@@ -391,6 +391,23 @@ def test_quantized_matmul_irregular(dev, fmt, m, k, n, group):
     _qmatmul_case(dev, fmt, m, k, n, group, seed=m + k + n + group)
 
 
+@pytest.mark.parametrize("fmt", [orc.INT4, orc.INT8])
+@pytest.mark.parametrize("m,k,n,group", [
+    (1, 640, 1040, 128),     # 5 warp-steps per row, a ragged last row block
+    (3, 640, 1040, 128),
+    (1, 256, 16, 128),       # one row block shared by many CTAs
+    (2, 1024, 48, 256),      # group spanning two warp-steps (INT4)
+    (32, 4096, 1024, 128),   # activation windows shorter than the row
+    (17, 14336, 512, 128),   # three n-tiles, windows
+    (5, 8192, 2064, 128),
+])
+def test_quantized_matmul_tma_shapes(dev, fmt, m, k, n, group):
+    # The TMA-fed decode GEMV: ranges that split row blocks across CTAs
+    # (partial slots + ticket), windows, ragged row blocks, both formats.
+    err = _qmatmul_case(dev, fmt, m, k, n, group, seed=m * 13 + k + n + group)
+    assert err < 1e-4 * max(1.0, (k / 4096) ** 0.5), err
+
+
 @pytest.mark.parametrize("fmt,k,n", [(orc.INT4, 14336, 4096), (orc.INT4, 4096, 14336),
                                      (orc.INT8, 8192, 1024)])
 def test_quantized_matmul_full_size_spot_rows(dev, fmt, k, n):
