@@ -121,10 +121,9 @@ int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, u
                               ? SLC_OK : SLC_ERR_EXECUTION;
     // NCCL gathers rank blocks contiguously ([world][rows][cols]); with one
     // row that already is [rows, world * cols], otherwise interleave.
-    // Staging after the GEMV tickets, inside the kernel-scratch region.
-    const uint64_t ticket_bytes = 64 * 1024 * sizeof(unsigned);
-    float *dst = rows == 1 ? out : reinterpret_cast<float *>(d->workspace + ticket_bytes);
-    if (rows > 1 && world * rows * cols * sizeof(float) > d->workspace_bytes / 2 - ticket_bytes)
+    // Staging in the kernel-scratch region of the workspace.
+    float *dst = rows == 1 ? out : reinterpret_cast<float *>(ws_scratch(d));
+    if (rows > 1 && world * rows * cols * sizeof(float) > ws_scratch_bytes(d))
         return SLC_ERR_EXECUTION;
     ncclResult_t r = api().all_gather(in, dst, rows * cols, ncclFloat32, d->comm->comm, d->stream);
     slc::k::count_launch();

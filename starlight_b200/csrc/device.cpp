@@ -455,6 +455,10 @@ extern "C" int slc_fill_normal(slc_device *d, slc_buffer_ref out, uint64_t seed,
         return invalid_range(d, out.buffer, out.offset, out.len);
     cudaError_t e = k::fill_normal(d->stream, reinterpret_cast<float *>(b->ptr) + out.offset, out.len,
                                    seed, offset, mean, stdev);
+    // Completes before returning: the quantized GEMV streams weights (codes
+    // and scales) ahead of its predecessor kernel, so nothing that writes
+    // them may still be running when a dispatch is enqueued.
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     return e == cudaSuccess ? SLC_OK : cuda_err(d, e);
 }
 
@@ -544,6 +548,8 @@ extern "C" int slc_quantize(slc_device *d, slc_buffer_ref weights, uint64_t rows
     cudaError_t e = k::quantize(d->stream, reinterpret_cast<const float *>(wb->ptr) + weights.offset,
                                 rows, kk, group, (int)format, reinterpret_cast<uint8_t *>(cb->ptr),
                                 reinterpret_cast<float *>(sb->ptr));
+    // Completes before returning (see slc_fill_normal).
+    if (e == cudaSuccess) e = cudaStreamSynchronize(d->stream);
     if (e != cudaSuccess) return cuda_err(d, e);
     d->quant[codes_buffer] = QuantBinding{scales_buffer, format, group};
     return SLC_OK;

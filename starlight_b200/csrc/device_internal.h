@@ -42,6 +42,25 @@ struct slc_device {
     CommState *comm = nullptr;
 };
 
+// Device workspace layout (reserved once at creation; dispatch never
+// allocates). W = workspace_bytes.
+//   [0, 256 KiB)              split-K tickets of the quantized GEMV
+//   [256 KiB, W/2 - 64 KiB)   kernel scratch, used by one kernel at a time:
+//                             GEMV partial sums, attention chunk partials,
+//                             all-gather staging
+//   [W/2 - 64 KiB, W/2)       tickets of the decode attention
+//   [W/2, W)                  operator intermediates (SwiGlu, RmsNormMatMul)
+// Tickets start at zero and every kernel that takes one resets it.
+constexpr uint64_t kGemvTicketBytes = 64 * 1024 * sizeof(unsigned);
+constexpr uint64_t kAttnTicketBytes = 16 * 1024 * sizeof(unsigned);
+inline char *ws_scratch(slc_device *d) { return d->workspace + kGemvTicketBytes; }
+inline uint64_t ws_scratch_bytes(slc_device *d) {
+    return d->workspace_bytes / 2 - kAttnTicketBytes - kGemvTicketBytes;
+}
+inline unsigned *ws_attn_tickets(slc_device *d) {
+    return reinterpret_cast<unsigned *>(d->workspace + d->workspace_bytes / 2 - kAttnTicketBytes);
+}
+
 // Error helpers shared by the operator layer.
 int slc_fail(slc_device *d, int status, const char *msg);
 int slc_fail_buffer(slc_device *d, uint32_t buffer);

@@ -21,10 +21,22 @@
 //
 // Decode is HBM-bound on the KV read: algorithmic bytes per layer
 // 2 * 4 * batch * kv_heads * (past_len + 1) * head_dim (+ q and out).
+//
+// Decode (seq == 1, head_dim 64 or 128, up to 8 query heads per KV head)
+// has its own kernel, attention_decode: the append and the attention are
+// one launch (the CTA whose chunk holds the new key reads it from the k / v
+// inputs and writes it to the cache), each lane owns head_dim / 32
+// consecutive dimensions of every GQA query row and of the K / V rows it
+// streams (128-bit loads, 4 keys per warp in flight), scores are warp sums,
+// and the chunks of one (batch, kv_head) are merged in ascending order by the
+// last CTA to finish (atomic ticket, no waiting). With a device-resident
+// past_len (graph replay) the grid is planned for max_seq and chunks beyond
+// the live keys only take their ticket.
 #include <math.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "tma.cuh"
 
 namespace slc {
 namespace k {
@@ -40,7 +52,17 @@ __global__ void __launch_bounds__(256) kv_append_kernel(const float *__restrict_
                                                         size_t layers, size_t layer,
                                                         size_t kv_heads, size_t head_dim,
                                                         size_t max_seq, size_t past_len,
-                                                        size_t seq) {
+                                                        size_t seq, const uint32_t *d_past,
+                                                        uint32_t *err) {
+    pdl_trigger();
+    pdl_wait();
+    if (d_past) {
+        past_len = *d_past;
+        if (past_len + seq > max_seq) {  // validated on the host; guard anyway
+            report_error(err, kErrBadScalar);
+            return;
+        }
+    }
     const size_t time_stride = kv_heads * head_dim;
     const size_t parity_stride = max_seq * time_stride;
     const size_t layer_stride = 2 * parity_stride;
@@ -68,9 +90,12 @@ struct AttnParams {
     size_t batch_stride, parity_stride, time_stride;
     size_t group, g_block, t_block, chunk_keys, chunks;
     float scale;
+    const uint32_t *d_past;  // device past_len (graph replay) or null
 };
 
 __global__ void __launch_bounds__(kThreads) attention_kernel(AttnParams p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float smem[];
     const size_t D = p.head_dim;
     const int R_MAX = kMaxRows;
@@ -94,8 +119,9 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(AttnParams p) {
     const size_t tn = min(p.t_block, p.seq - t0);
     const int rows = (int)(gn * tn);  // row r = tq * gn + gi
 
+    const size_t past_len = p.d_past ? (size_t)*p.d_past : p.past_len;
     const size_t key_begin = chunk * p.chunk_keys;
-    const size_t last_key = p.past_len + t0 + tn - 1;  // largest visible key of this CTA
+    const size_t last_key = past_len + t0 + tn - 1;  // largest visible key of this CTA
     size_t key_end = min(key_begin + p.chunk_keys, last_key + 1);
 
     // Load the query rows.
@@ -130,7 +156,7 @@ __global__ void __launch_bounds__(kThreads) attention_kernel(AttnParams p) {
         for (int i = threadIdx.x; i < rows * kTileKeys; i += kThreads) {
             int r = i / kTileKeys, j = i - r * kTileKeys;
             size_t tq = (size_t)r / gn;
-            size_t limit = p.past_len + t0 + tq;  // keys 0..=limit visible
+            size_t limit = past_len + t0 + tq;  // keys 0..=limit visible
             float sc = -INFINITY;
             if (j < tk && j0 + j <= limit) {
                 const float *qr = q_s + (size_t)r * D;
@@ -193,6 +219,8 @@ __global__ void __launch_bounds__(128) attention_combine(const float *__restrict
                                                          const float *__restrict__ part_ml,
                                                          float *__restrict__ out, size_t rows,
                                                          size_t chunks, size_t head_dim) {
+    pdl_trigger();
+    pdl_wait();
     for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float *ml = part_ml + row * chunks * 2;
         float m = -INFINITY;
@@ -242,42 +270,378 @@ Plan plan(size_t batch, size_t heads, size_t kv_heads, size_t seq, size_t past_l
     return pl;
 }
 
+
+// ---- decode -------------------------------------------------------------------
+
+constexpr int kDecThreads = 128;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kDecMaxGroup = 8;
+constexpr int kDecKeysPerWarp = 4;  // keys in flight per warp
+constexpr int kDecMaxChunks = 512;  // chunks per (batch, kv_head)
+
+struct DecodeParams {
+    const float *q;        // [B, H, 1, D]
+    const float *k_new;    // [B, Hkv, 1, D]
+    const float *v_new;
+    float *cache;
+    float *out;            // [B, H, 1, D]
+    float *part_o;         // [B * H][chunks][D]
+    float *part_ml;        // [B * H][chunks][2]
+    unsigned *tickets;     // [B * Hkv]
+    const uint32_t *d_past;  // device past_len (graph replay) or null
+    uint32_t *err;
+    long long batch_stride, layer_off, parity_stride, time_stride;
+    int past, max_seq;
+    int H, Hkv, G, chunk_keys, chunks;
+    float scale;
+};
+
+template <int VEC>
+struct Vec;
+template <>
+struct Vec<2> {
+    using T = float2;
+    __device__ static T ld(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+    __device__ static void st(float *p, T v) { *reinterpret_cast<float2 *>(p) = v; }
+    __device__ static float dot(T a, T b) { return fmaf(a.y, b.y, a.x * b.x); }
+    __device__ static void axpby(T &o, float a, float p, T v) {
+        o.x = fmaf(p, v.x, o.x * a);
+        o.y = fmaf(p, v.y, o.y * a);
+    }
+    __device__ static float get(T v, int i) { return i == 0 ? v.x : v.y; }
+    __device__ static void set(T &v, int i, float x) { (i == 0 ? v.x : v.y) = x; }
+    __device__ static T zero() { return make_float2(0.f, 0.f); }
+};
+template <>
+struct Vec<4> {
+    using T = float4;
+    __device__ static T ld(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+    __device__ static void st(float *p, T v) { *reinterpret_cast<float4 *>(p) = v; }
+    __device__ static float dot(T a, T b) {
+        return fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
+    }
+    __device__ static void axpby(T &o, float a, float p, T v) {
+        o.x = fmaf(p, v.x, o.x * a);
+        o.y = fmaf(p, v.y, o.y * a);
+        o.z = fmaf(p, v.z, o.z * a);
+        o.w = fmaf(p, v.w, o.w * a);
+    }
+    __device__ static float get(T v, int i) {
+        return i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w));
+    }
+    __device__ static void set(T &v, int i, float x) {
+        (i == 0 ? v.x : (i == 1 ? v.y : (i == 2 ? v.z : v.w))) = x;
+    }
+    __device__ static T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) {
+    pdl_trigger();
+    pdl_wait();
+    using V = Vec<VEC>;
+    using T = typename V::T;
+    constexpr int D = 32 * VEC;
+    __shared__ float sm_o[kDecWarps][kDecMaxGroup][D];
+    __shared__ float sm_ml[kDecWarps][kDecMaxGroup][2];
+    __shared__ int is_last;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int bh = blockIdx.y, chunk = blockIdx.x;
+    const int b = bh / p.Hkv, kvh = bh - b * p.Hkv;
+    const int G = p.G;
+    int past = p.past;
+    if (p.d_past) {
+        past = (int)*p.d_past;
+        if (past < 0 || past >= p.max_seq) {  // validated on the host; guard anyway
+            report_error(p.err, kErrBadScalar);
+            past = 0;
+        }
+    }
+    const int n_keys = past + 1;
+    const int k0 = chunk * p.chunk_keys;
+    const int k1 = min(n_keys, k0 + p.chunk_keys);
+
+    // Query rows of the group (lane slice), pre-scaled.
+    T q[kDecMaxGroup];
+#pragma unroll
+    for (int r = 0; r < kDecMaxGroup; r++) {
+        q[r] = V::zero();
+        if (r < G) {
+            const float *qr = p.q + ((long long)(b * p.H + kvh * G + r)) * D + lane * VEC;
+            q[r] = V::ld(qr);
+#pragma unroll
+            for (int i = 0; i < VEC; i++) V::set(q[r], i, V::get(q[r], i) * p.scale);
+        }
+    }
+    float m[kDecMaxGroup], l[kDecMaxGroup];
+    T o[kDecMaxGroup];
+#pragma unroll
+    for (int r = 0; r < kDecMaxGroup; r++) {
+        m[r] = -INFINITY;
+        l[r] = 0.f;
+        o[r] = V::zero();
+    }
+
+    const float *kbase = p.cache + b * p.batch_stride + p.layer_off + (long long)kvh * D + lane * VEC;
+    const float *knew = p.k_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
+    const float *vnew = p.v_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
+    for (int j0 = k0 + warp; j0 < k1; j0 += kDecWarps * kDecKeysPerWarp) {
+        T kv[kDecKeysPerWarp], vv[kDecKeysPerWarp];
+        int nk = 0;
+#pragma unroll
+        for (int i = 0; i < kDecKeysPerWarp; i++) {
+            const int j = j0 + i * kDecWarps;
+            kv[i] = V::zero();
+            vv[i] = V::zero();
+            if (j < k1) {
+                nk = i + 1;
+                if (j == past) {
+                    // The new key: from the inputs, appended to the cache
+                    // (attention.rs:61-78 index arithmetic).
+                    kv[i] = V::ld(knew);
+                    vv[i] = V::ld(vnew);
+                    float *dst = const_cast<float *>(kbase) + (long long)j * p.time_stride;
+                    V::st(dst, kv[i]);
+                    V::st(dst + p.parity_stride, vv[i]);
+                } else {
+                    const float *src = kbase + (long long)j * p.time_stride;
+                    kv[i] = V::ld(src);
+                    vv[i] = V::ld(src + p.parity_stride);
+                }
+            }
+        }
+        // Scores of this warp's keys for every query row.
+        float sc[kDecKeysPerWarp][kDecMaxGroup];
+#pragma unroll
+        for (int i = 0; i < kDecKeysPerWarp; i++)
+#pragma unroll
+            for (int r = 0; r < kDecMaxGroup; r++)
+                sc[i][r] = (r < G && i < nk) ? warp_sum(V::dot(q[r], kv[i])) : -INFINITY;
+#pragma unroll
+        for (int r = 0; r < kDecMaxGroup; r++) {
+            if (r < G) {
+                float mb = sc[0][r];
+#pragma unroll
+                for (int i = 1; i < kDecKeysPerWarp; i++) mb = fmaxf(mb, sc[i][r]);
+                const float m_new = fmaxf(m[r], mb);
+                const float alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new);
+                float lsum = l[r] * alpha;
+                T acc = o[r];
+#pragma unroll
+                for (int i = 0; i < VEC; i++) V::set(acc, i, V::get(acc, i) * alpha);
+#pragma unroll
+                for (int i = 0; i < kDecKeysPerWarp; i++) {
+                    const float pj = sc[i][r] == -INFINITY ? 0.f : expf(sc[i][r] - m_new);
+                    lsum += pj;
+                    V::axpby(acc, 1.0f, pj, vv[i]);
+                }
+                o[r] = acc;
+                l[r] = lsum;
+                m[r] = m_new;
+            }
+        }
+    }
+
+    // Merge the warps (ascending warp order) into the CTA's partial.
+#pragma unroll
+    for (int r = 0; r < kDecMaxGroup; r++) {
+        if (r < G) {
+#pragma unroll
+            for (int i = 0; i < VEC; i++) sm_o[warp][r][lane * VEC + i] = V::get(o[r], i);
+            if (lane == 0) {
+                sm_ml[warp][r][0] = m[r];
+                sm_ml[warp][r][1] = l[r];
+            }
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
+        const int r = idx / D, d = idx - r * D;
+        float mm = -INFINITY;
+        for (int w = 0; w < kDecWarps; w++) mm = fmaxf(mm, sm_ml[w][r][0]);
+        float ll = 0.f, acc = 0.f;
+        for (int w = 0; w < kDecWarps; w++) {
+            const float mw = sm_ml[w][r][0];
+            if (mw != -INFINITY) {
+                const float f = expf(mw - mm);
+                ll = fmaf(sm_ml[w][r][1], f, ll);
+                acc = fmaf(sm_o[w][r][d], f, acc);
+            }
+        }
+        const long long row = (long long)b * p.H + kvh * G + r;
+        if (p.chunks == 1) {
+            p.out[row * D + d] = __fdiv_rn(acc, ll);
+        } else {
+            p.part_o[(row * p.chunks + chunk) * D + d] = acc;
+            if (d == 0) {
+                p.part_ml[(row * p.chunks + chunk) * 2 + 0] = mm;
+                p.part_ml[(row * p.chunks + chunk) * 2 + 1] = ll;
+            }
+        }
+    }
+    if (p.chunks == 1) return;
+
+    // Last CTA of this (batch, kv_head) merges the chunks in ascending order.
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned ticket = atomicAdd(&p.tickets[bh], 1u);
+        is_last = ticket == (unsigned)(p.chunks - 1);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    // Chunk weights exp(m_c - M) / L per query row, computed once in shared
+    // memory (the chunk statistics are loaded in parallel), then every
+    // (row, dim) output adds the live chunks in ascending order.
+    __shared__ float sm_w[kDecMaxGroup][kDecMaxChunks];
+    __shared__ float sm_inv[kDecMaxGroup];
+    const int live = min(p.chunks, (n_keys + p.chunk_keys - 1) / p.chunk_keys);
+    const long long row0 = (long long)b * p.H + kvh * G;
+    for (int i = threadIdx.x; i < G * live; i += kDecThreads) {
+        const int r = i / live, c = i - r * live;
+        sm_w[r][c] = __ldcg(p.part_ml + ((row0 + r) * p.chunks + c) * 2);
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+        const int r = threadIdx.x;
+        float mm = -INFINITY;
+        for (int c = 0; c < live; c++) mm = fmaxf(mm, sm_w[r][c]);
+        float ll = 0.f;
+        for (int c = 0; c < live; c++) {
+            const float mc = sm_w[r][c];
+            const float f = mc == -INFINITY ? 0.f : expf(mc - mm);
+            ll = fmaf(__ldcg(p.part_ml + ((row0 + r) * p.chunks + c) * 2 + 1), f, ll);
+            sm_w[r][c] = f;
+        }
+        sm_inv[r] = ll;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
+        const int r = idx / D, d = idx - r * D;
+        const float *po = p.part_o + (row0 + r) * p.chunks * D + d;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int c = 0; c < live; c++) acc = fmaf(__ldcg(po + (long long)c * D), sm_w[r][c], acc);
+        p.out[(row0 + r) * D + d] = __fdiv_rn(acc, sm_inv[r]);
+    }
+    if (threadIdx.x == 0) p.tickets[bh] = 0u;  // ready for the next launch
+}
+
+struct DecodePlan {
+    bool ok = false;
+    int chunk_keys = 0, chunks = 0;
+};
+
+// keys_max: the most keys any replay can see (past_len + 1 for a host
+// scalar, max_seq for a device-resident one).
+DecodePlan plan_decode(size_t batch, size_t kv_heads, size_t heads, size_t seq, size_t head_dim,
+                       size_t keys_max) {
+    DecodePlan pl;
+    if (seq != 1 || kv_heads == 0 || heads % kv_heads != 0) return pl;
+    const size_t group = heads / kv_heads;
+    if (group > (size_t)kDecMaxGroup || (head_dim != 64 && head_dim != 128)) return pl;
+    if (keys_max > (size_t)INT32_MAX || batch * kv_heads > 65535) return pl;
+    const size_t bh = batch * kv_heads;
+    // About two CTAs per SM, each at least 32 keys.
+    size_t want = (2 * (size_t)kSmCount + bh - 1) / bh;
+    size_t by_len = (keys_max + 31) / 32;
+    size_t chunks = want < by_len ? want : by_len;
+    if (chunks < 1) chunks = 1;
+    size_t ck = (keys_max + chunks - 1) / chunks;
+    ck = (ck + 15) / 16 * 16;
+    pl.chunk_keys = (int)ck;
+    pl.chunks = (int)((keys_max + ck - 1) / ck);
+    if (pl.chunks > kDecMaxChunks) {  // very long contexts: larger chunks
+        ck = (keys_max + kDecMaxChunks - 1) / kDecMaxChunks;
+        ck = (ck + 15) / 16 * 16;
+        pl.chunk_keys = (int)ck;
+        pl.chunks = (int)((keys_max + ck - 1) / ck);
+    }
+    pl.ok = true;
+    return pl;
+}
+
 }  // namespace
 
 cudaError_t kv_append(cudaStream_t s, const float *k, const float *v, float *cache,
-                      const KvGeometry &g, size_t past_len, size_t seq) {
+                      const KvGeometry &g, size_t past_len, size_t seq, const uint32_t *d_past) {
     size_t total = g.batch * g.kv_heads * seq * g.head_dim;
     if (total == 0) return cudaSuccess;
-    kv_append_kernel<<<grid_for(total, 256), 256, 0, s>>>(k, v, cache, g.batch, g.layers, g.layer,
+    launch_k(kv_append_kernel, grid_for(total, 256), 256, 0, s, k, v, cache, g.batch, g.layers, g.layer,
                                                           g.kv_heads, g.head_dim, g.max_seq,
-                                                          past_len, seq);
+                                                          past_len, seq, d_past, nullptr);
     count_launch();
     return cudaGetLastError();
 }
 
 size_t attention_workspace_bytes(size_t batch, size_t heads, size_t kv_heads, size_t seq,
-                                 size_t past_len, size_t head_dim) {
+                                 size_t past_len, size_t head_dim, size_t max_seq,
+                                 bool device_past) {
     if (seq == 0 || batch == 0 || kv_heads == 0) return 0;
-    Plan pl = plan(batch, heads, kv_heads, seq, past_len, head_dim);
+    const size_t keys = device_past ? max_seq : past_len + seq;
+    DecodePlan dp = plan_decode(batch, kv_heads, heads, seq, head_dim, keys);
+    if (dp.ok) return dp.chunks <= 1 ? 0 : batch * heads * dp.chunks * (head_dim + 2) * 4;
+    Plan pl = plan(batch, heads, kv_heads, seq, keys - seq, head_dim);
     if (pl.chunks <= 1) return 0;
     return batch * heads * seq * pl.chunks * (head_dim + 2) * sizeof(float);
 }
 
 cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, const float *v,
                              float *cache, float *out, const KvGeometry &g, size_t heads,
-                             size_t seq, size_t past_len, float scale, void *workspace,
-                             size_t workspace_bytes) {
-    cudaError_t e = kv_append(s, k, v, cache, g, past_len, seq);
-    if (e != cudaSuccess || seq == 0 || g.batch == 0) return e;
-    Plan pl = plan(g.batch, heads, g.kv_heads, seq, past_len, g.head_dim);
+                             size_t seq, size_t past_len, float scale, const AttnScratch &scr,
+                             const uint32_t *d_past) {
+    if (seq == 0 || g.batch == 0) return kv_append(s, k, v, cache, g, past_len, seq, d_past);
+    const size_t keys = d_past ? g.max_seq : past_len + seq;
+    const size_t time_stride = g.kv_heads * g.head_dim;
+    const size_t parity_stride = g.max_seq * time_stride;
+    DecodePlan dp = plan_decode(g.batch, g.kv_heads, heads, seq, g.head_dim, keys);
+    if (dp.ok && g.batch * g.kv_heads <= scr.ticket_count) {
+        const size_t need = dp.chunks <= 1 ? 0 : g.batch * heads * dp.chunks * (g.head_dim + 2) * 4;
+        if (need > scr.workspace_bytes) return cudaErrorMemoryAllocation;
+        DecodeParams p{};
+        p.q = q;
+        p.k_new = k;
+        p.v_new = v;
+        p.cache = cache;
+        p.out = out;
+        p.part_o = static_cast<float *>(scr.workspace);
+        p.part_ml = p.part_o + g.batch * heads * dp.chunks * g.head_dim;
+        p.tickets = scr.tickets;
+        p.d_past = d_past;
+        p.err = scr.err;
+        p.batch_stride = (long long)(g.layers * 2 * parity_stride);
+        p.layer_off = (long long)(g.layer * 2 * parity_stride);
+        p.parity_stride = (long long)parity_stride;
+        p.time_stride = (long long)time_stride;
+        p.past = (int)past_len;
+        p.max_seq = (int)g.max_seq;
+        p.H = (int)heads;
+        p.Hkv = (int)g.kv_heads;
+        p.G = (int)(heads / g.kv_heads);
+        p.chunk_keys = dp.chunk_keys;
+        p.chunks = dp.chunks;
+        p.scale = scale;
+        dim3 grid((unsigned)dp.chunks, (unsigned)(g.batch * g.kv_heads));
+        if (g.head_dim == 128)
+            launch_k(attention_decode<4>, grid, kDecThreads, 0, s, p);
+        else
+            launch_k(attention_decode<2>, grid, kDecThreads, 0, s, p);
+        count_launch();
+        return cudaGetLastError();
+    }
+    cudaError_t e = kv_append(s, k, v, cache, g, past_len, seq, d_past);
+    if (e != cudaSuccess) return e;
+    Plan pl = plan(g.batch, heads, g.kv_heads, seq, keys - seq, g.head_dim);
     size_t rows = g.batch * heads * seq;
     size_t need = rows * pl.chunks * (g.head_dim + 2) * sizeof(float);
-    if (pl.chunks > 1 && need > workspace_bytes) return cudaErrorMemoryAllocation;
+    if (pl.chunks > 1 && need > scr.workspace_bytes) return cudaErrorMemoryAllocation;
     AttnParams p{};
     p.q = q;
     p.cache = cache;
     p.out = out;
-    p.part_o = static_cast<float *>(workspace);
+    p.part_o = static_cast<float *>(scr.workspace);
     p.part_ml = p.part_o + rows * pl.chunks * g.head_dim;
     p.batch = g.batch;
     p.heads = heads;
@@ -285,8 +649,8 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
     p.seq = seq;
     p.past_len = past_len;
     p.head_dim = g.head_dim;
-    p.time_stride = g.kv_heads * g.head_dim;
-    p.parity_stride = g.max_seq * p.time_stride;
+    p.time_stride = time_stride;
+    p.parity_stride = parity_stride;
     p.key_base_layer = g.layer * 2 * p.parity_stride;
     p.batch_stride = g.layers * 2 * p.parity_stride;
     p.group = heads / g.kv_heads;
@@ -295,6 +659,7 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
     p.chunk_keys = pl.chunk_keys;
     p.chunks = pl.chunks;
     p.scale = scale;
+    p.d_past = d_past;
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -302,10 +667,10 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
         configured = true;
     }
     dim3 grid((unsigned)pl.chunks, (unsigned)pl.grid_y, (unsigned)(g.batch * g.kv_heads));
-    attention_kernel<<<grid, kThreads, pl.smem, s>>>(p);
+    launch_k(attention_kernel, grid, kThreads, pl.smem, s, p);
     count_launch();
     if (pl.chunks > 1) {
-        attention_combine<<<grid_for(rows, 1, 16), 128, 0, s>>>(p.part_o, p.part_ml, out, rows,
+        launch_k(attention_combine, grid_for(rows, 1, 16), 128, 0, s, p.part_o, p.part_ml, out, rows,
                                                                 pl.chunks, g.head_dim);
         count_launch();
     }

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace slc {
 
 // B200: 148 SMs on two dies. Grids of memory-bound kernels are sized as a
@@ -56,6 +58,41 @@ __device__ __forceinline__ float ld_cg_f32(const float *p) {
 
 __host__ __device__ __forceinline__ bool aligned16(const void *p) {
     return (reinterpret_cast<uintptr_t>(p) & 15u) == 0;
+}
+
+// Programmatic dependent launch. Every kernel lets the next kernel of its
+// stream launch as soon as all of its own CTAs are resident (pdl_trigger),
+// and waits for the previous kernel's completion and memory before its first
+// access to data another kernel produced (pdl_wait). Without the launch
+// attribute both are no-ops.
+__device__ __forceinline__ void pdl_trigger() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+namespace k {
+// Whether launches on this thread may overlap their predecessor (on by
+// default; entry points that run on a caller's stream turn it off).
+bool pdl_enabled();
+void set_pdl_enabled(bool on);
+}  // namespace k
+
+// Launches `kernel` on `s`, with programmatic stream serialization when
+// enabled, so its prologue overlaps the previous kernel's tail.
+template <typename... Params, typename... Args>
+cudaError_t launch_k(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                     cudaStream_t s, Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = k::pdl_enabled() ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Host-side helpers.

@@ -16,6 +16,11 @@ namespace k {
 
 static std::atomic<uint64_t> g_launches{0};
 uint64_t launch_count() { return g_launches.load(); }
+namespace {
+thread_local bool t_pdl = true;
+}
+bool pdl_enabled() { return t_pdl; }
+void set_pdl_enabled(bool on) { t_pdl = on; }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 namespace {
@@ -37,6 +42,8 @@ template <Op OP>
 __global__ void __launch_bounds__(256) ew_vec(const float *__restrict__ a,
                                               const float *__restrict__ b, float f,
                                               float *__restrict__ out, size_t n4) {
+    pdl_trigger();
+    pdl_wait();
     size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
         float4 x = ld_stream_f4(a + 4 * i);
@@ -56,6 +63,8 @@ __global__ void __launch_bounds__(256) ew_scalar(const float *__restrict__ a,
                                                  const float *__restrict__ b, float f,
                                                  float *__restrict__ out, size_t begin,
                                                  size_t n) {
+    pdl_trigger();
+    pdl_wait();
     size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = begin + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         float y = 0.f;
@@ -72,11 +81,11 @@ cudaError_t launch(cudaStream_t s, const float *a, const float *b, float f, floa
                  (b ? reinterpret_cast<uintptr_t>(b) : 0)) & 15u) == 0;
     size_t n4 = vec ? n / 4 : 0;
     if (n4) {
-        ew_vec<OP><<<grid_for(n4, 256), 256, 0, s>>>(a, b, f, out, n4);
+        launch_k(ew_vec<OP>, grid_for(n4, 256), 256, 0, s, a, b, f, out, n4);
         count_launch();
     }
     if (n4 * 4 < n) {
-        ew_scalar<OP><<<grid_for(n - n4 * 4, 256), 256, 0, s>>>(a, b, f, out, n4 * 4, n);
+        launch_k(ew_scalar<OP>, grid_for(n - n4 * 4, 256), 256, 0, s, a, b, f, out, n4 * 4, n);
         count_launch();
     }
     return cudaGetLastError();
@@ -87,6 +96,8 @@ __global__ void __launch_bounds__(256) add_bias_kernel(const float *__restrict__
                                                        const float *__restrict__ bias,
                                                        float *__restrict__ out, size_t rows,
                                                        size_t cols, bool vec) {
+    pdl_trigger();
+    pdl_wait();
     size_t stride = (size_t)gridDim.x * blockDim.x;
     if (vec) {
         size_t c4 = cols / 4, n4 = rows * c4;
@@ -135,7 +146,7 @@ cudaError_t add_bias(cudaStream_t s, const float *a, const float *b, const float
                ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
                  reinterpret_cast<uintptr_t>(bias) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
     size_t work = vec ? rows * cols / 4 : rows * cols;
-    add_bias_kernel<<<grid_for(work, 256), 256, 0, s>>>(a, b, bias, out, rows, cols, vec);
+    launch_k(add_bias_kernel, grid_for(work, 256), 256, 0, s, a, b, bias, out, rows, cols, vec);
     count_launch();
     return cudaGetLastError();
 }

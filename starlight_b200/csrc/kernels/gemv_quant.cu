@@ -62,6 +62,8 @@ struct GemvArgs {
 
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kThreads) qgemv_mma(GemvArgs p) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ __align__(16) unsigned char smem_raw[];
     constexpr int KSTEP = Fmt<FMT>::kStep;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -283,6 +285,8 @@ __global__ void __launch_bounds__(256) qgemv_simple(const float *__restrict__ x,
                                                     size_t row_bytes,
                                                     const float *__restrict__ scales, int group,
                                                     int groups, float *__restrict__ out, int N) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * 8;
     for (int n = blockIdx.x * 8 + (threadIdx.x >> 5); n < N; n += warps) {
@@ -318,6 +322,8 @@ __global__ void __launch_bounds__(256) qgemv_simple(const float *__restrict__ x,
 __global__ void __launch_bounds__(256) quant_scales(const float *__restrict__ w, size_t n,
                                                     size_t k, size_t group, size_t groups,
                                                     float qmax, float *__restrict__ scales) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     size_t total = n * groups, warps = (size_t)gridDim.x * 8;
     for (size_t i = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); i < total; i += warps) {
@@ -342,6 +348,8 @@ __global__ void __launch_bounds__(256) quant_codes(const float *__restrict__ w, 
                                                    size_t row_bytes, int format, float qmax,
                                                    const float *__restrict__ scales,
                                                    uint8_t *__restrict__ codes) {
+    pdl_trigger();
+    pdl_wait();
     size_t total = n * row_bytes, stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         size_t row = i / row_bytes, b = i - row * row_bytes;
@@ -363,6 +371,8 @@ __global__ void __launch_bounds__(256) dequant_kernel(const uint8_t *__restrict_
                                                       size_t n, size_t k, size_t group,
                                                       size_t groups, size_t row_bytes,
                                                       int format, float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     size_t total = n * k, stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         size_t row = i / k, c = i - row * k;
@@ -453,7 +463,7 @@ cudaError_t launch_fast(cudaStream_t s, const float *x, size_t m, const QuantWei
         configured[FMT][NT] = true;
     }
     dim3 grid((unsigned)pl.row_blocks, (unsigned)pl.ksplit);
-    qgemv_mma<FMT, NT><<<grid, kThreads, pl.smem, s>>>(a);
+    launch_k(qgemv_mma<FMT, NT>, grid, kThreads, pl.smem, s, a);
     count_launch();
     return cudaGetLastError();
 }
@@ -518,11 +528,11 @@ cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight 
         } else {
             int grid = grid_for(w.n, 8, 16);
             if (w.format == 0)
-                qgemv_simple<0><<<grid, 256, 0, s>>>(xb, (int)mb, (int)w.k, w.codes, w.row_bytes,
+                launch_k(qgemv_simple<0>, grid, 256, 0, s, xb, (int)mb, (int)w.k, w.codes, w.row_bytes,
                                                      w.scales, (int)w.group, (int)w.groups, ob,
                                                      (int)w.n);
             else
-                qgemv_simple<1><<<grid, 256, 0, s>>>(xb, (int)mb, (int)w.k, w.codes, w.row_bytes,
+                launch_k(qgemv_simple<1>, grid, 256, 0, s, xb, (int)mb, (int)w.k, w.codes, w.row_bytes,
                                                      w.scales, (int)w.group, (int)w.groups, ob,
                                                      (int)w.n);
             count_launch();
@@ -539,9 +549,9 @@ cudaError_t quantize(cudaStream_t s, const float *w, size_t n, size_t k, size_t 
     const size_t groups = (k + group - 1) / group;
     const size_t row_bytes = format == 0 ? (k + 1) / 2 : k;
     const float qmax = format == 0 ? 7.0f : 127.0f;
-    quant_scales<<<grid_for(n * groups, 8, 16), 256, 0, s>>>(w, n, k, group, groups, qmax, scales);
+    launch_k(quant_scales, grid_for(n * groups, 8, 16), 256, 0, s, w, n, k, group, groups, qmax, scales);
     count_launch();
-    quant_codes<<<grid_for(n * row_bytes, 256), 256, 0, s>>>(w, n, k, group, groups, row_bytes,
+    launch_k(quant_codes, grid_for(n * row_bytes, 256), 256, 0, s, w, n, k, group, groups, row_bytes,
                                                              format, qmax, scales, codes);
     count_launch();
     return cudaGetLastError();
@@ -549,7 +559,7 @@ cudaError_t quantize(cudaStream_t s, const float *w, size_t n, size_t k, size_t 
 
 cudaError_t dequantize(cudaStream_t s, const QuantWeight &w, float *out) {
     if (w.n == 0 || w.k == 0) return cudaSuccess;
-    dequant_kernel<<<grid_for(w.n * w.k, 256), 256, 0, s>>>(w.codes, w.scales, w.n, w.k, w.group,
+    launch_k(dequant_kernel, grid_for(w.n * w.k, 256), 256, 0, s, w.codes, w.scales, w.n, w.k, w.group,
                                                             w.groups, w.row_bytes, w.format, out);
     count_launch();
     return cudaGetLastError();

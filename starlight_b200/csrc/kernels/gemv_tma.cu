@@ -318,6 +318,10 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     const long long grid = gridDim.x, cta = blockIdx.x;
     const long long u0 = cta * p.total / grid, u1 = (cta + 1) * p.total / grid;
 
+    // The producer streams weights before the previous kernel has finished
+    // (weights are written only by uploads and quantization, which complete
+    // before any dispatch); consumers wait for it before reading x.
+    pdl_trigger();
     if (threadIdx.x == 0) {
         for (int i = 0; i < p.nstage; i++) {
             mbar_init(&full[i], 1);
@@ -365,6 +369,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     }
 
     // ---- consumers.
+    pdl_wait();
     stage_x<FMT, CW>(p, xh, xl, unscale);
     float res[NT][4];
     int slot = 0, phase = 0;
@@ -456,9 +461,11 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
                 const int rows_here = min(kBlockRows, p.N - (int)blk * kBlockRows);
                 for (int i = threadIdx.x; i < Mc * rows_here; i += CW * 32) {
                     const int c = i / rows_here, r = (int)blk * kBlockRows + i % rows_here;
+                    const float *src = p.partials + (long long)c * p.N + r;
+                    const long long slot_stride = (long long)Mc * p.N;
                     float v = 0.f;
-                    for (int sl = 0; sl < count; sl++)
-                        v += ld_cg_f32(p.partials + ((long long)sl * Mc + c) * p.N + r);
+#pragma unroll 8
+                    for (int sl = 0; sl < count; sl++) v += __ldcg(src + sl * slot_stride);
                     p.out[(size_t)c * p.N + r] = v;
                 }
                 if (threadIdx.x == 0) p.tickets[blk] = 0u;  // ready for the next launch
@@ -591,7 +598,7 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, size_t m, const QuantWeig
                              kSmemLimit);
         configured = true;
     }
-    qgemv_tma<FMT, NT, SPLIT><<<pl.grid, (kTiles * SPLIT + 1) * 32, pl.smem, s>>>(a);
+    launch_k(qgemv_tma<FMT, NT, SPLIT>, pl.grid, (kTiles * SPLIT + 1) * 32, pl.smem, s, a);
     count_launch();
     return cudaGetLastError();
 }

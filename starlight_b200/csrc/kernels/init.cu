@@ -24,6 +24,8 @@ __host__ __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
 __global__ void __launch_bounds__(256) fill_normal_kernel(float *__restrict__ out, size_t n,
                                                           uint64_t seed, uint64_t offset,
                                                           float mean, float std) {
+    pdl_trigger();
+    pdl_wait();
     size_t stride = (size_t)gridDim.x * blockDim.x;
     const uint64_t key = splitmix64(seed);
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -40,7 +42,7 @@ __global__ void __launch_bounds__(256) fill_normal_kernel(float *__restrict__ ou
 cudaError_t fill_normal(cudaStream_t s, float *out, size_t n, uint64_t seed, uint64_t offset,
                         float mean, float std) {
     if (n == 0) return cudaSuccess;
-    fill_normal_kernel<<<grid_for(n, 256), 256, 0, s>>>(out, n, seed, offset, mean, std);
+    launch_k(fill_normal_kernel, grid_for(n, 256), 256, 0, s, out, n, seed, offset, mean, std);
     count_launch();
     return cudaGetLastError();
 }

@@ -52,14 +52,26 @@ struct KvGeometry {
     size_t batch, layers, layer, kv_heads, head_dim, max_seq;
 };
 cudaError_t kv_append(cudaStream_t s, const float *k, const float *v, float *cache,
-                      const KvGeometry &g, size_t past_len, size_t seq);
-// Workspace needed by causal_attention for the given shape (bytes).
+                      const KvGeometry &g, size_t past_len, size_t seq,
+                      const uint32_t *d_past = nullptr);
+// Workspace needed by causal_attention for the given shape (bytes);
+// device_past: past_len will be read from device memory (planned for max_seq).
 size_t attention_workspace_bytes(size_t batch, size_t heads, size_t kv_heads, size_t seq,
-                                 size_t past_len, size_t head_dim);
+                                 size_t past_len, size_t head_dim, size_t max_seq,
+                                 bool device_past);
+struct AttnScratch {
+    void *workspace;        // chunk partials
+    size_t workspace_bytes;
+    unsigned *tickets;      // zeroed, reset by the kernels
+    size_t ticket_count;
+    uint32_t *err;          // device error word
+};
+// Appends k / v at past_len and attends (attention.rs:129-219). d_past, if
+// set, is a device copy of past_len (read by the kernels).
 cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, const float *v,
                              float *cache, float *out, const KvGeometry &g, size_t heads,
-                             size_t seq, size_t past_len, float scale, void *workspace,
-                             size_t workspace_bytes);
+                             size_t seq, size_t past_len, float scale, const AttnScratch &scr,
+                             const uint32_t *d_past = nullptr);
 
 // ---- matmul_f32.cu --------------------------------------------------------------
 // out[b] = a[b or 0] . w[b or 0]^T (NT) or a . w (NN), batch broadcast when a

@@ -53,6 +53,8 @@ __device__ __forceinline__ bool source_row(const RowMap &m, size_t r, size_t *sr
 __global__ void __launch_bounds__(256) copy_rows_vec(const float *__restrict__ src,
                                                      float *__restrict__ dst, size_t rows,
                                                      size_t width, RowMap m) {
+    pdl_trigger();
+    pdl_wait();
     const size_t w4 = width / 4, total = rows * w4;
     size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -66,6 +68,8 @@ __global__ void __launch_bounds__(256) copy_rows_vec(const float *__restrict__ s
 __global__ void __launch_bounds__(256) copy_rows(const float *__restrict__ src,
                                                  float *__restrict__ dst, size_t rows,
                                                  size_t width, RowMap m) {
+    pdl_trigger();
+    pdl_wait();
     const size_t total = rows * width;
     size_t stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
@@ -79,9 +83,9 @@ cudaError_t launch(cudaStream_t s, const float *src, float *dst, size_t rows, si
                    const RowMap &m) {
     if (rows == 0 || width == 0) return cudaSuccess;
     if (width % 4 == 0 && aligned16(src) && aligned16(dst))
-        copy_rows_vec<<<grid_for(rows * width / 4, 256), 256, 0, s>>>(src, dst, rows, width, m);
+        launch_k(copy_rows_vec, grid_for(rows * width / 4, 256), 256, 0, s, src, dst, rows, width, m);
     else
-        copy_rows<<<grid_for(rows * width, 256), 256, 0, s>>>(src, dst, rows, width, m);
+        launch_k(copy_rows, grid_for(rows * width, 256), 256, 0, s, src, dst, rows, width, m);
     count_launch();
     return cudaGetLastError();
 }
@@ -116,6 +120,8 @@ namespace {
 __global__ void __launch_bounds__(256) interleave_kernel(const float *__restrict__ src,
                                                          float *__restrict__ dst, size_t blocks,
                                                          size_t rows, size_t cols) {
+    pdl_trigger();
+    pdl_wait();
     size_t total = blocks * rows * cols, stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
         size_t c = i % cols, br = i / cols, r = br % rows, b = br / rows;
@@ -128,7 +134,7 @@ cudaError_t interleave_blocks(cudaStream_t s, const float *src, float *dst, size
                               size_t rows, size_t cols) {
     size_t total = blocks * rows * cols;
     if (total == 0) return cudaSuccess;
-    interleave_kernel<<<grid_for(total, 256), 256, 0, s>>>(src, dst, blocks, rows, cols);
+    launch_k(interleave_kernel, grid_for(total, 256), 256, 0, s, src, dst, blocks, rows, cols);
     count_launch();
     return cudaGetLastError();
 }

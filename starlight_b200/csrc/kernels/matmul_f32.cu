@@ -22,6 +22,8 @@ __global__ void __launch_bounds__(256) sgemm_kernel(const float *__restrict__ a,
                                                     float *__restrict__ out, size_t m, size_t k,
                                                     size_t n, size_t a_bstride,
                                                     size_t w_bstride) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float As[BK][BM + 4];
     __shared__ float Ws[BK][BN + 4];
     const size_t bz = blockIdx.z;
@@ -84,6 +86,8 @@ __global__ void __launch_bounds__(256) qgemm_kernel(const float *__restrict__ a,
                                                    float *__restrict__ out, size_t m, size_t k,
                                                    size_t n, size_t row_bytes, size_t group,
                                                    size_t groups) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float As[BK][BM + 4];
     __shared__ float Ws[BK][BN + 4];
     const size_t m0 = (size_t)blockIdx.y * BM, n0 = (size_t)blockIdx.x * BN;
@@ -145,10 +149,10 @@ cudaError_t qgemm_f32(cudaStream_t s, const float *a, size_t m, const QuantWeigh
     if (m == 0 || w.n == 0) return cudaSuccess;
     dim3 grid((unsigned)((w.n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM));
     if (w.format == 0)
-        qgemm_kernel<0><<<grid, 256, 0, s>>>(a, w.codes, w.scales, out, m, w.k, w.n, w.row_bytes,
+        launch_k(qgemm_kernel<0>, grid, 256, 0, s, a, w.codes, w.scales, out, m, w.k, w.n, w.row_bytes,
                                              w.group, w.groups);
     else
-        qgemm_kernel<1><<<grid, 256, 0, s>>>(a, w.codes, w.scales, out, m, w.k, w.n, w.row_bytes,
+        launch_k(qgemm_kernel<1>, grid, 256, 0, s, a, w.codes, w.scales, out, m, w.k, w.n, w.row_bytes,
                                              w.group, w.groups);
     count_launch();
     return cudaGetLastError();
@@ -171,9 +175,9 @@ cudaError_t matmul_f32(cudaStream_t s, const float *a, const float *w, float *ou
     }
     dim3 grid((unsigned)((n + BN - 1) / BN), (unsigned)((m + BM - 1) / BM), (unsigned)batch);
     if (transposed)
-        sgemm_kernel<true><<<grid, 256, 0, s>>>(a, w, out, m, k, n, a_bs, w_bs);
+        launch_k(sgemm_kernel<true>, grid, 256, 0, s, a, w, out, m, k, n, a_bs, w_bs);
     else
-        sgemm_kernel<false><<<grid, 256, 0, s>>>(a, w, out, m, k, n, a_bs, w_bs);
+        launch_k(sgemm_kernel<false>, grid, 256, 0, s, a, w, out, m, k, n, a_bs, w_bs);
     count_launch();
     return cudaGetLastError();
 }

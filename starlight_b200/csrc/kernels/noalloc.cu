@@ -19,6 +19,7 @@
 #include <mutex>
 
 #include "../../../include/starlight_cuda.h"
+#include "common.cuh"
 #include "kernels.h"
 
 namespace {
@@ -104,7 +105,12 @@ extern "C" int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes
     // The tickets must start at zero; a previous call may have been cut short.
     if (need > 0 && cudaMemsetAsync(scratch, 0, kTicketBytes, s) != cudaSuccess)
         return fail(error_message, SLC_ERR_EXECUTION, "clearing the scratch tickets failed");
+    // The caller's stream may have just written the weights: no launch
+    // overlap with the previous kernel.
+    const bool pdl = slc::k::pdl_enabled();
+    slc::k::set_pdl_enabled(false);
     cudaError_t e = slc::k::qmatmul(s, x, m, w, out, scratch, kScratchBytes);
+    slc::k::set_pdl_enabled(pdl);
     if (e != cudaSuccess) return fail(error_message, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
     return SLC_OK;
 }

@@ -26,6 +26,8 @@ __global__ void __launch_bounds__(256) rms_norm_regs(const float *__restrict__ x
                                                      const float *__restrict__ w,
                                                      float *__restrict__ out, size_t rows,
                                                      size_t hidden, float eps) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float partial[8];
     const size_t h4 = hidden / 4;
     for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
@@ -69,6 +71,8 @@ __global__ void __launch_bounds__(256) rms_norm_warp(const float *__restrict__ x
                                                      const float *__restrict__ w,
                                                      float *__restrict__ out, size_t rows,
                                                      size_t hidden, float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     size_t warps = (size_t)gridDim.x * 8;
     for (size_t row = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += warps) {
@@ -86,6 +90,8 @@ __global__ void __launch_bounds__(256) rms_norm_generic(const float *__restrict_
                                                         const float *__restrict__ w,
                                                         float *__restrict__ out, size_t rows,
                                                         size_t hidden, float eps) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float partial[8];
     for (size_t row = blockIdx.x; row < rows; row += gridDim.x) {
         const float *xr = x + row * hidden;
@@ -108,6 +114,8 @@ __global__ void __launch_bounds__(256) rms_norm_generic(const float *__restrict_
 __global__ void __launch_bounds__(256) rms_inverse_kernel(const float *__restrict__ x,
                                                           float *__restrict__ inv, size_t rows,
                                                           size_t hidden, float eps) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     size_t warps = (size_t)gridDim.x * 8;
     for (size_t row = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += warps) {
@@ -124,6 +132,8 @@ __global__ void __launch_bounds__(256) rms_apply_kernel(const float *__restrict_
                                                         const float *__restrict__ w,
                                                         float *__restrict__ out, size_t rows,
                                                         size_t hidden) {
+    pdl_trigger();
+    pdl_wait();
     size_t n = rows * hidden, stride = (size_t)gridDim.x * blockDim.x;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
         size_t r = i / hidden, c = i - r * hidden;
@@ -140,17 +150,17 @@ cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out,
     size_t h4 = hidden / 4;
     int grid = (int)(rows < (size_t)kSmCount * 16 ? rows : (size_t)kSmCount * 16);
     if (hidden <= 1024 && rows >= 64) {
-        rms_norm_warp<<<grid_for(rows, 8, 16), 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_warp, grid_for(rows, 8, 16), 256, 0, s, x, w, out, rows, hidden, eps);
     } else if (vec && h4 <= 256) {
-        rms_norm_regs<1><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<1>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     } else if (vec && h4 <= 512) {
-        rms_norm_regs<2><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<2>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     } else if (vec && h4 <= 1024) {
-        rms_norm_regs<4><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<4>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     } else if (vec && h4 <= 2048) {
-        rms_norm_regs<8><<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<8>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     } else {
-        rms_norm_generic<<<grid, 256, 0, s>>>(x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_generic, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     }
     count_launch();
     return cudaGetLastError();
@@ -159,7 +169,7 @@ cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out,
 cudaError_t rms_inverse(cudaStream_t s, const float *x, float *inv, size_t rows, size_t hidden,
                         float eps) {
     if (rows == 0) return cudaSuccess;
-    rms_inverse_kernel<<<grid_for(rows, 8, 16), 256, 0, s>>>(x, inv, rows, hidden, eps);
+    launch_k(rms_inverse_kernel, grid_for(rows, 8, 16), 256, 0, s, x, inv, rows, hidden, eps);
     count_launch();
     return cudaGetLastError();
 }
@@ -167,7 +177,7 @@ cudaError_t rms_inverse(cudaStream_t s, const float *x, float *inv, size_t rows,
 cudaError_t rms_apply(cudaStream_t s, const float *x, const float *inv, const float *w,
                       float *out, size_t rows, size_t hidden) {
     if (rows == 0) return cudaSuccess;
-    rms_apply_kernel<<<grid_for(rows * hidden, 256), 256, 0, s>>>(x, inv, w, out, rows, hidden);
+    launch_k(rms_apply_kernel, grid_for(rows * hidden, 256), 256, 0, s, x, inv, w, out, rows, hidden);
     count_launch();
     return cudaGetLastError();
 }

@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(256) softmax_regs(const float *__restrict__ x,
                                                     float *__restrict__ out, size_t rows,
                                                     size_t cols, size_t seq, size_t past,
                                                     bool causal) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const size_t c4 = cols / 4;
     size_t warps = (size_t)gridDim.x * 8;
@@ -73,6 +75,8 @@ __global__ void __launch_bounds__(256) softmax_generic(const float *__restrict__
                                                        float *__restrict__ out, size_t rows,
                                                        size_t cols, size_t seq, size_t past,
                                                        bool causal) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     size_t warps = (size_t)gridDim.x * 8;
     for (size_t row = (size_t)blockIdx.x * 8 + (threadIdx.x >> 5); row < rows; row += warps) {
@@ -97,17 +101,17 @@ cudaError_t launch(cudaStream_t s, const float *x, float *out, size_t rows, size
     bool vec = cols % 4 == 0 && aligned16(x) && aligned16(out);
     size_t per_lane = (cols / 4 + 31) / 32;
     if (vec && per_lane <= 1)
-        softmax_regs<1><<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_regs<1>, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     else if (vec && per_lane <= 2)
-        softmax_regs<2><<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_regs<2>, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     else if (vec && per_lane <= 4)
-        softmax_regs<4><<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_regs<4>, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     else if (vec && per_lane <= 8)
-        softmax_regs<8><<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_regs<8>, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     else if (vec && per_lane <= 16)
-        softmax_regs<16><<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_regs<16>, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     else
-        softmax_generic<<<grid, 256, 0, s>>>(x, out, rows, cols, seq, past, causal);
+        launch_k(softmax_generic, grid, 256, 0, s, x, out, rows, cols, seq, past, causal);
     count_launch();
     return cudaGetLastError();
 }

@@ -26,6 +26,7 @@ struct Cmd {
     const uint32_t *scalars;
     uint64_t n_scalars;
     int64_t state_index;
+    const uint32_t *dyn_scalars;  // device copies of the scalars (graph replay) or null
 };
 
 struct Dims {
@@ -205,16 +206,12 @@ bool state_geometry(Checker &ck, const Dims &st, uint64_t batch, uint64_t kv_hea
     return true;
 }
 
-// Workspace layout: [0, 256 KiB) holds the split-K tickets of the quantized
-// GEMV (zeroed at creation, reset by every last CTA, never used by anything
-// else); [256 KiB, W/2) is kernel-internal scratch (GEMV split-K partials,
-// attention chunk partials, the all-gather staging); [W/2, W) holds operator
-// intermediates (SwiGlu gate/up rows, normalised rows of RmsNormMatMul).
-constexpr uint64_t kTicketBytes = 64 * 1024 * sizeof(unsigned);
+// Workspace regions: see device_internal.h. The GEMV gets the tickets and
+// the scratch behind them (partials at +256 KiB).
 void *gemv_workspace(slc_device *d) { return d->workspace; }
-uint64_t gemv_workspace_bytes(slc_device *d) { return d->workspace_bytes / 2; }
-void *kernel_scratch(slc_device *d) { return d->workspace + kTicketBytes; }
-uint64_t kernel_scratch_bytes(slc_device *d) { return d->workspace_bytes / 2 - kTicketBytes; }
+uint64_t gemv_workspace_bytes(slc_device *d) { return d->workspace_bytes / 2 - kAttnTicketBytes; }
+void *kernel_scratch(slc_device *d) { return ws_scratch(d); }
+uint64_t kernel_scratch_bytes(slc_device *d) { return ws_scratch_bytes(d); }
 float *intermediates(slc_device *d) {
     return reinterpret_cast<float *>(d->workspace + d->workspace_bytes / 2);
 }
@@ -525,14 +522,16 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
         if (heads % kvh != 0) return ck.exec("heads must be a multiple of kv_heads");
         if (past + sq > max_seq) return ck.exec("past_len + seq exceeds max_seq");
         if (hd > 384) return ck.fail(SLC_ERR_UNIMPLEMENTED, "causal_attention supports head_dim <= 384");
-        uint64_t need = k::attention_workspace_bytes(b, heads, kvh, sq, past, hd);
+        uint64_t need = k::attention_workspace_bytes(b, heads, kvh, sq, past, hd, max_seq,
+                                                     c.dyn_scalars != nullptr);
         if (need > kernel_scratch_bytes(d))
             return ck.exec("device workspace is too small for this attention shape");
         if (!launch) return SLC_OK;
         k::KvGeometry g{b, layers, layer, kvh, hd, max_seq};
+        k::AttnScratch scr{kernel_scratch(d), kernel_scratch_bytes(d), ws_attn_tickets(d),
+                           kAttnTicketBytes / sizeof(unsigned), d->device_flag};
         return finish(ck, k::causal_attention(s, qp, kp, vp, ck.state(), ck.output(), g, heads, sq,
-                                              past, c.op->scale, kernel_scratch(d),
-                                              kernel_scratch_bytes(d)));
+                                              past, c.op->scale, scr, c.dyn_scalars));
     }
     case SLC_OP_SWIGLU: {
         Dims x, g, u, dn, o;
@@ -646,7 +645,7 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
 Cmd make_cmd(const slc_op *op, const slc_buffer_ref *in, const slc_value *iv, uint64_t n_in,
              const slc_buffer_ref *out, const slc_value *ov, uint64_t n_out,
              const uint32_t *scalars, uint64_t n_scalars) {
-    Cmd c{op, in, iv, n_in, out, ov, n_out, scalars, n_scalars, -1};
+    Cmd c{op, in, iv, n_in, out, ov, n_out, scalars, n_scalars, -1, nullptr};
     for (uint64_t i = 0; i < n_in; i++)
         if (iv[i].role == SLC_ROLE_STATE) c.state_index = (int64_t)i;
     return c;

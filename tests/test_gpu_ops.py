@@ -215,8 +215,15 @@ ATTN_CASES = [
     # 8B decode shape, GQA 4:1, long past (split-K with combine)
     (17, dict(batch=1, layers=2, layer=1, heads=32, kv_heads=8, seq=1, past_len=1279, head_dim=128, max_seq=1280)),
     (18, dict(batch=4, layers=1, layer=0, heads=32, kv_heads=8, seq=1, past_len=300, head_dim=128, max_seq=512)),
+    # decode kernel (seq 1, head_dim 64/128, up to 8 query heads per KV head):
+    # one key, one chunk, GQA 2/8, long pasts split over many chunks
+    (21, dict(batch=1, layers=1, layer=0, heads=8, kv_heads=8, seq=1, past_len=0, head_dim=64, max_seq=4)),
+    (22, dict(batch=3, layers=2, layer=0, heads=64, kv_heads=8, seq=1, past_len=777, head_dim=128, max_seq=800)),
+    (23, dict(batch=1, layers=1, layer=0, heads=4, kv_heads=2, seq=1, past_len=17, head_dim=64, max_seq=20)),
+    (24, dict(batch=2, layers=3, layer=2, heads=16, kv_heads=2, seq=1, past_len=2047, head_dim=128, max_seq=2048)),
+    (25, dict(batch=1, layers=1, layer=0, heads=4, kv_heads=4, seq=1, past_len=63, head_dim=64, max_seq=64)),
     # prefill chunk with a past
-    (19, dict(batch=1, layers=1, layer=0, heads=8, kv_heads=2, seq=40, past_len=9, head_dim=64, max_seq=64)),
+    (19,dict(batch=1, layers=1, layer=0, heads=8, kv_heads=2, seq=40, past_len=9, head_dim=64, max_seq=64)),
     (20, dict(batch=2, layers=1, layer=0, heads=4, kv_heads=4, seq=33, past_len=0, head_dim=64, max_seq=40)),
 ]
 
