@@ -279,18 +279,26 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
                          [Value.f32((batch, k)), val], [BufferRef(outs[n], 0, batch * n)],
                          [Value.f32((batch, n))])
 
-    run_all()
-    dev.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 3
-    with torch.cuda.stream(stream):
+
+    def timed(segment):
+        # With capture on, the third and later runs of the same segment are
+        # one CUDA-graph replay: the events then bracket device work only.
+        for _ in range(3):
+            segment()
+            dev.flush()
+            dev.synchronize()
         t0.record(stream)
         for _ in range(reps):
-            run_all()
+            segment()
+            dev.flush()
         t1.record(stream)
-    dev.synchronize()
-    t1.synchronize()
-    ms = t0.elapsed_time(t1)
+        dev.synchronize()
+        t1.synchronize()
+        return t0.elapsed_time(t1)
+
+    ms = timed(run_all)
 
     def algo_bytes(val):
         n, k = val.shape
@@ -315,16 +323,7 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
                 dev.dispatch(Op(OpCode.MatMulNT), [BufferRef(xbufs[k], 0, batch * k), ref],
                              [Value.f32((batch, k)), val], [BufferRef(outs[n], 0, batch * n)],
                              [Value.f32((batch, n))])
-        run_subset()
-        dev.synchronize()
-        with torch.cuda.stream(stream):
-            t0.record(stream)
-            for _ in range(reps):
-                run_subset()
-            t1.record(stream)
-        dev.synchronize()
-        t1.synchronize()
-        us = t0.elapsed_time(t1) * 1e3 / (reps * len(subset))
+        us = timed(run_subset) * 1e3 / (reps * len(subset))
         b = algo_bytes(subset[0][1])
         shapes[key] = {"launch_us": round(us, 2), "gbs": round(b / us / 1e3, 1),
                        "frac": round(b / us / 1e3 / peak[0], 3), "launches": len(subset)}
@@ -357,14 +356,19 @@ def rmsnorm_gbs(dev, peak):
                      [Value.f32((rows, h)), Value.f32((h,), ValueRole.Param)],
                      [BufferRef(outs[i % 2], 0, rows * h)], [Value.f32((rows, h))])
 
-    for i in range(4):
-        one(i)
-    dev.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     reps = 32
+
+    def segment():
+        for i in range(reps):
+            one(i)
+        dev.flush()
+
+    for _ in range(3):  # eager, captured, replayed (with capture on)
+        segment()
+        dev.synchronize()
     t0.record(stream)
-    for i in range(reps):
-        one(i)
+    segment()
     t1.record(stream)
     dev.synchronize()
     t1.synchronize()
@@ -382,6 +386,8 @@ def run_ours(args, dist: Dist):
     world, rank = dist.world, dist.rank
     torch.cuda.set_device(dist.local)
     dev = CudaDevice(dist.local)
+    # Command capture: repeated decode steps replay as one CUDA graph each.
+    dev.set_capture(True)
     if world > 1:
         uid = comm_unique_id() if rank == 0 else None
         uid = dist.broadcast_bytes(uid, 128)
@@ -450,6 +456,7 @@ def run_ours(args, dist: Dist):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * 4 * B,
                     "d2h_bytes_per_step": 4 * B * V},
             "gpu_launches": launches,
+            "capture": dev.capture_stats(),
             "roofline": roof,
             "norm": norm,
             "weight_bytes_per_rank": model.weight_bytes(),

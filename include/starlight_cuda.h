@@ -252,12 +252,24 @@ int slc_device_stream(slc_device *device, void **out_stream);
 uint64_t slc_kernel_launch_count(const slc_device *device);
 
 /* ---- EXTENSION: command capture and replay -------------------------------
- * With capture enabled, dispatches between two synchronize points are
- * recorded; when the same sequence of operators on the same buffer ranges
- * repeats (only scalar operands such as past_len may change), synchronize
- * replays it as one CUDA graph launch with the new scalars instead of
- * launching every kernel again. Semantics are unchanged. Off by default. */
+ * With capture enabled, dispatches are validated as usual (errors are still
+ * returned by slc_dispatch) but their launches are deferred until the next
+ * call that makes their effects observable (synchronize, flush, upload,
+ * download, ...). When the same sequence of operators on the same buffer
+ * ranges repeats (only the seq_len / past_len scalars of LastToken,
+ * KvAppend and CausalAttention may change), it is replayed as one CUDA graph
+ * launch with the new scalars: captured the second time it is seen, replayed
+ * from the third. Results are those of eager execution. Off by default. */
 int slc_set_capture(slc_device *device, int enabled);
+/* Submits deferred work to the device stream without waiting for it. */
+int slc_flush(slc_device *device);
+typedef struct {
+    uint64_t captures;           /* graphs captured */
+    uint64_t replays;            /* graph replays */
+    uint64_t replayed_commands;  /* commands executed inside graphs */
+    uint64_t eager_commands;     /* commands launched one by one */
+} slc_capture_info;
+int slc_capture_stats(const slc_device *device, slc_capture_info *out);
 
 /* ---- EXTENSION: tensor parallelism over NCCL -----------------------------
  * slc_comm_unique_id fills 128 bytes on one rank (an ncclUniqueId) that the

@@ -1,24 +1,300 @@
-// Command capture and CUDA-graph replay for backend-cuda (see slc_set_capture
-// in include/starlight_cuda.h).
+// Command capture and CUDA-graph replay (slc_set_capture).
+//
+// With capture on, slc_dispatch validates a command exactly as before (every
+// error is still reported by the dispatch call itself) and records it instead
+// of launching it. The recorded segment runs at the next point where its
+// effects could be observed (synchronize, upload, download, flush, any other
+// call that touches the stream or device data):
+//
+//  * the segment's key is everything that determines its kernels: operators
+//    and their attributes, buffer references, values, and the scalars of
+//    operators that cannot take them from device memory. The scalars of
+//    LastToken, KvAppend and CausalAttention (seq_len, past_len) are not part
+//    of the key: their kernels read them from a device table, written from
+//    pinned host memory before each replay;
+//  * the first time a key is seen the segment runs eagerly (launch by
+//    launch); the second time it is captured into a CUDA graph (kernels read
+//    the table) and instantiated; from then on it is replayed with one graph
+//    launch. Up to kMaxGraphs graphs are kept (least recently used evicted).
+//    A segment that fails to capture runs eagerly and is not tried again.
+//
+// Results are those of eager execution: the same kernels run on the same
+// buffers in the same order. Graphs hold device pointers, so the cache is
+// dropped whenever a buffer is released or a quantization binding changes.
+#include <cuda_runtime.h>
+#include <string.h>
+
+#include <algorithm>
+#include <list>
+#include <unordered_map>
+#include <vector>
+
 #include "device_internal.h"
 
-struct CaptureState {
-    bool enabled = false;
+namespace {
+
+constexpr size_t kMaxGraphs = 8;
+constexpr uint32_t kTableSlots = 1 << 14;  // device scalars per segment
+constexpr size_t kMaxPorts = 8;
+
+struct Rec {
+    slc_op op;
+    uint32_t n_in, n_out, n_scalars;
+    slc_buffer_ref in[kMaxPorts], out[kMaxPorts];
+    slc_value iv[kMaxPorts], ov[kMaxPorts];
+    uint32_t scalars[kMaxPorts];
+    int32_t slot;  // first device-table slot of its scalars, or -1
 };
+
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    std::vector<unsigned char> key;
+    uint64_t launches = 0;  // kernels per replay
+};
+
+bool dynamic_scalars(uint16_t code) {
+    return code == SLC_OP_LAST_TOKEN || code == SLC_OP_KV_APPEND ||
+           code == SLC_OP_CAUSAL_ATTENTION;
+}
+
+uint64_t fnv1a(const unsigned char *p, size_t n) {
+    uint64_t h = 1469598103934665603ull;
+    for (size_t i = 0; i < n; i++) h = (h ^ p[i]) * 1099511628211ull;
+    return h;
+}
+
+}  // namespace
+
+struct CaptureState {
+    std::vector<Rec> pending;
+    std::vector<unsigned char> key;
+    uint32_t table_used = 0;
+    uint32_t *h_table = nullptr;  // pinned
+    uint32_t *d_table = nullptr;
+    cudaEvent_t table_done = nullptr;
+    bool table_pending = false;
+    std::unordered_map<uint64_t, std::list<Graph>::iterator> by_hash;
+    std::list<Graph> graphs;  // front = most recently used
+    std::unordered_map<uint64_t, int> seen;  // key hash -> times run (-1: never capture)
+    slc_capture_info stats{};
+};
+
+static void append_key(CaptureState *cs, const void *p, size_t n) {
+    const unsigned char *b = static_cast<const unsigned char *>(p);
+    cs->key.insert(cs->key.end(), b, b + n);
+}
+
+static void drop_graphs(CaptureState *cs) {
+    for (Graph &g : cs->graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    cs->graphs.clear();
+    cs->by_hash.clear();
+}
+
+void invalidate_capture(slc_device *d) {
+    if (d->capture) drop_graphs(d->capture);
+}
 
 extern "C" int slc_set_capture(slc_device *d, int enabled) {
     if (!d) return SLC_ERR_EXECUTION;
-    (void)enabled;
-    return slc_fail(d, SLC_ERR_UNIMPLEMENTED, "command capture is not available in this build");
+    int rc = flush_capture(d);
+    if (rc != SLC_OK) return rc;
+    if (!enabled) {
+        release_capture(d);
+        return SLC_OK;
+    }
+    if (d->capture) return SLC_OK;
+    cudaSetDevice(d->ordinal);
+    CaptureState *cs = new (std::nothrow) CaptureState();
+    if (!cs) return slc_fail(d, SLC_ERR_OUT_OF_MEMORY, "capture state allocation failed");
+    if (cudaMallocHost(&cs->h_table, kTableSlots * sizeof(uint32_t)) != cudaSuccess ||
+        cudaMalloc(&cs->d_table, kTableSlots * sizeof(uint32_t)) != cudaSuccess ||
+        cudaEventCreateWithFlags(&cs->table_done, cudaEventDisableTiming) != cudaSuccess) {
+        if (cs->h_table) cudaFreeHost(cs->h_table);
+        if (cs->d_table) cudaFree(cs->d_table);
+        delete cs;
+        return slc_fail(d, SLC_ERR_OUT_OF_MEMORY, "capture scalar table allocation failed");
+    }
+    cs->pending.reserve(1024);
+    cs->key.reserve(1 << 20);
+    d->capture = cs;
+    return SLC_OK;
 }
 
-int flush_capture(slc_device *) { return SLC_OK; }
+extern "C" int slc_capture_stats(const slc_device *d, slc_capture_info *out) {
+    if (!d || !out) return SLC_ERR_EXECUTION;
+    *out = d->capture ? d->capture->stats : slc_capture_info{};
+    return SLC_OK;
+}
+
 void release_capture(slc_device *d) {
-    delete d->capture;
+    CaptureState *cs = d->capture;
+    if (!cs) return;
+    cudaSetDevice(d->ordinal);
+    cudaStreamSynchronize(d->stream);
+    drop_graphs(cs);
+    if (cs->h_table) cudaFreeHost(cs->h_table);
+    if (cs->d_table) cudaFree(cs->d_table);
+    if (cs->table_done) cudaEventDestroy(cs->table_done);
+    delete cs;
     d->capture = nullptr;
 }
-int capture_record(slc_device *, const slc_op *, const slc_buffer_ref *, const slc_value *,
-                   uint64_t, const slc_buffer_ref *, const slc_value *, uint64_t,
-                   const uint32_t *, uint64_t) {
-    return 0;
+
+int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
+                   const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
+                   const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
+                   uint64_t n_scalars) {
+    CaptureState *cs = d->capture;
+    const bool dyn = dynamic_scalars(op->code);
+    if (n_in > kMaxPorts || n_out > kMaxPorts || n_scalars > kMaxPorts ||
+        (dyn && cs->table_used + n_scalars > kTableSlots)) {
+        // Not recordable: run what is pending, then this command eagerly.
+        flush_capture(d);
+        return 0;
+    }
+    Rec r;
+    memset(&r, 0, sizeof(r));  // the key is built from raw bytes
+    r.op = *op;
+    r.n_in = (uint32_t)n_in;
+    r.n_out = (uint32_t)n_out;
+    r.n_scalars = (uint32_t)n_scalars;
+    for (uint64_t i = 0; i < n_in; i++) {
+        r.in[i] = in[i];
+        r.in[i].reserved = 0;
+        r.iv[i] = iv[i];
+    }
+    for (uint64_t i = 0; i < n_out; i++) {
+        r.out[i] = out[i];
+        r.out[i].reserved = 0;
+        r.ov[i] = ov[i];
+    }
+    for (uint64_t i = 0; i < n_scalars; i++) r.scalars[i] = scalars[i];
+    r.slot = -1;
+    if (dyn && n_scalars) {
+        r.slot = (int32_t)cs->table_used;
+        cs->table_used += (uint32_t)n_scalars;
+    }
+    // Key: everything but the values of dynamic scalars.
+    append_key(cs, &r.op, sizeof(r.op));
+    append_key(cs, &r.n_in, sizeof(uint32_t) * 3);
+    append_key(cs, r.in, sizeof(slc_buffer_ref) * n_in);
+    append_key(cs, r.iv, sizeof(slc_value) * n_in);
+    append_key(cs, r.out, sizeof(slc_buffer_ref) * n_out);
+    append_key(cs, r.ov, sizeof(slc_value) * n_out);
+    if (!dyn) append_key(cs, r.scalars, sizeof(uint32_t) * n_scalars);
+    cs->pending.push_back(r);
+    return 1;
+}
+
+// Runs the pending commands launch by launch; dyn = device table (capture).
+static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
+    for (const Rec &r : cs->pending) {
+        const uint32_t *ds = (dyn && r.slot >= 0) ? cs->d_table + r.slot : nullptr;
+        int rc = slc_launch_command(d, &r.op, r.in, r.iv, r.n_in, r.out, r.ov, r.n_out,
+                                    r.scalars, r.n_scalars, ds);
+        if (rc != SLC_OK) return rc;
+    }
+    return SLC_OK;
+}
+
+// Copies the segment's dynamic scalars to the device table (stream-ordered).
+static int upload_table(slc_device *d, CaptureState *cs) {
+    if (cs->table_used == 0) return SLC_OK;
+    // The previous copy must have read the pinned table before it changes.
+    if (cs->table_pending && cudaEventSynchronize(cs->table_done) != cudaSuccess)
+        return slc_fail(d, SLC_ERR_EXECUTION, "capture scalar table synchronization failed");
+    for (const Rec &r : cs->pending)
+        if (r.slot >= 0)
+            memcpy(cs->h_table + r.slot, r.scalars, sizeof(uint32_t) * r.n_scalars);
+    if (cudaMemcpyAsync(cs->d_table, cs->h_table, sizeof(uint32_t) * cs->table_used,
+                        cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+        cudaEventRecord(cs->table_done, d->stream) != cudaSuccess)
+        return slc_fail(d, SLC_ERR_EXECUTION, "capture scalar table upload failed");
+    cs->table_pending = true;
+    return SLC_OK;
+}
+
+static bool try_capture(slc_device *d, CaptureState *cs, Graph *g) {
+    const uint64_t before = slc::k::launch_count();
+    if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int rc = run_pending(d, cs, true);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t end = cudaStreamEndCapture(d->stream, &graph);
+    const uint64_t launched = slc::k::launch_count() - before;
+    slc::k::add_launches(-(int64_t)launched);  // nothing ran yet
+    bool ok = rc == SLC_OK && end == cudaSuccess && graph;
+    if (ok && cudaGraphInstantiate(&g->exec, graph, 0) != cudaSuccess) ok = false;
+    if (graph) cudaGraphDestroy(graph);
+    if (!ok) {
+        cudaGetLastError();
+        g->exec = nullptr;
+        d->last = slc_error{};  // a failed capture is not the caller's error
+        return false;
+    }
+    g->launches = launched;
+    return true;
+}
+
+int flush_capture(slc_device *d) {
+    CaptureState *cs = d ? d->capture : nullptr;
+    if (!cs || cs->pending.empty()) return SLC_OK;
+    cudaSetDevice(d->ordinal);
+    const uint64_t h = fnv1a(cs->key.data(), cs->key.size());
+    int rc = SLC_OK;
+    auto it = cs->by_hash.find(h);
+    if (it != cs->by_hash.end() && it->second->key == cs->key) {
+        // Replay.
+        cs->graphs.splice(cs->graphs.begin(), cs->graphs, it->second);
+        Graph &g = cs->graphs.front();
+        rc = upload_table(d, cs);
+        if (rc == SLC_OK && cudaGraphLaunch(g.exec, d->stream) != cudaSuccess)
+            rc = slc_fail(d, SLC_ERR_EXECUTION, "CUDA graph launch failed");
+        if (rc == SLC_OK) {
+            slc::k::add_launches((int64_t)g.launches);
+            cs->stats.replays++;
+            cs->stats.replayed_commands += cs->pending.size();
+        }
+    } else {
+        if (cs->seen.size() > 4096) cs->seen.clear();  // bound the history of keys
+        int &count = cs->seen[h];
+        bool captured = false;
+        if (count >= 1) {
+            Graph g;
+            g.key = cs->key;
+            rc = upload_table(d, cs);
+            if (rc == SLC_OK && try_capture(d, cs, &g)) {
+                if (cs->graphs.size() >= kMaxGraphs) {
+                    Graph &old = cs->graphs.back();
+                    cs->by_hash.erase(fnv1a(old.key.data(), old.key.size()));
+                    if (old.exec) cudaGraphExecDestroy(old.exec);
+                    cs->graphs.pop_back();
+                }
+                cs->graphs.push_front(std::move(g));
+                cs->by_hash[h] = cs->graphs.begin();
+                Graph &ng = cs->graphs.front();
+                if (cudaGraphLaunch(ng.exec, d->stream) != cudaSuccess) {
+                    rc = slc_fail(d, SLC_ERR_EXECUTION, "CUDA graph launch failed");
+                } else {
+                    slc::k::add_launches((int64_t)ng.launches);
+                    cs->stats.captures++;
+                    cs->stats.replayed_commands += cs->pending.size();
+                }
+                captured = true;
+            } else if (rc == SLC_OK) {
+                count = -1;  // does not capture; stay eager
+            }
+        }
+        if (!captured && rc == SLC_OK) {
+            if (count >= 0) count++;
+            rc = run_pending(d, cs, false);
+            cs->stats.eager_commands += cs->pending.size();
+        }
+    }
+    cs->pending.clear();
+    cs->key.clear();
+    cs->table_used = 0;
+    return rc;
 }

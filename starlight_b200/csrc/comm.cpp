@@ -75,6 +75,9 @@ extern "C" int slc_comm_init(slc_device *d, const uint8_t unique_id[128], int ra
     if (world < 1 || rank < 0 || rank >= world) return slc_fail(d, SLC_ERR_EXECUTION, "invalid rank");
     NcclApi &a = api();
     if (!a.ok) return slc_fail(d, SLC_ERR_UNIMPLEMENTED, "libnccl.so.2 could not be loaded");
+    int rc = flush_capture(d);
+    if (rc != SLC_OK) return rc;
+    invalidate_capture(d);  // graphs hold the communicator
     release_comm(d);
     ncclUniqueId id;
     memcpy(&id, unique_id, 128);

@@ -408,6 +408,11 @@ static int check_device_flag(slc_device *d) {
     }
 }
 
+extern "C" int slc_flush(slc_device *d) {
+    if (!d) return SLC_ERR_EXECUTION;
+    return flush_capture(d);
+}
+
 extern "C" int slc_synchronize(slc_device *d) {
     if (!d) return SLC_ERR_EXECUTION;
     int rc = flush_capture(d);
@@ -439,6 +444,7 @@ extern "C" int slc_release(slc_device *d, uint32_t buffer) {
     if (rc != SLC_OK) return rc;
     if (buffer >= d->buffers.size() || !d->buffers[buffer].alloc) return invalid_buffer(d, buffer);
     cudaStreamSynchronize(d->stream);
+    invalidate_capture(d);  // graphs hold device pointers
     cudaFree(d->buffers[buffer].alloc);
     d->buffers[buffer] = DeviceBuffer{};
     d->quant.erase(buffer);
@@ -482,6 +488,9 @@ extern "C" uint64_t slc_kernel_launch_count(const slc_device *) { return k::laun
 extern "C" int slc_bind_quant(slc_device *d, uint32_t codes_buffer, uint32_t scales_buffer,
                               uint32_t format, uint32_t group) {
     if (!d) return SLC_ERR_EXECUTION;
+    int rc = flush_capture(d);
+    if (rc != SLC_OK) return rc;
+    invalidate_capture(d);  // graphs hold quantization views
     if (!slot(d, codes_buffer, true)) return invalid_buffer(d, codes_buffer);
     if (!slot(d, scales_buffer, false)) return invalid_buffer(d, scales_buffer);
     if (format != SLC_QUANT_INT4 && format != SLC_QUANT_INT8)

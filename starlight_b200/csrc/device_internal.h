@@ -72,12 +72,15 @@ int slc_quant_view(slc_device *d, uint32_t codes_buffer, uint64_t offset_words, 
 // no-op when capture is off) and must run before any host-visible effect.
 int flush_capture(slc_device *d);
 void release_capture(slc_device *d);
-// Launch one validated command (used by the capture layer when replaying
-// eagerly). Returns an slc_status.
+// Drops captured graphs (they hold device pointers and quantization views).
+void invalidate_capture(slc_device *d);
+// Launch one validated command (used by the capture layer). dyn_scalars, if
+// set, is a device copy of `scalars` that the kernels read instead (graph
+// capture). Returns an slc_status.
 int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
                        const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
                        const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
-                       uint64_t n_scalars);
+                       uint64_t n_scalars, const uint32_t *dyn_scalars);
 // Try to record a validated command for graph replay. Returns 1 if the
 // command was recorded (launch deferred), 0 if it must be launched now.
 int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

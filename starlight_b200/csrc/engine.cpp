@@ -594,6 +594,8 @@ extern "C" int slc_llama_step(slc_llama *m, int mode, const uint32_t *ids,
                           r.ov.data(), r.out.size(), sc, r.scalar_src.size());
         if (rc != SLC_OK) return rc;
     }
+    // Deferred (captured) work goes to the stream before the end event.
+    if ((rc = slc_flush(d)) != SLC_OK) return rc;
     cudaEventRecord(m->ev_end, d->stream);
     if ((rc = slc_synchronize(d)) != SLC_OK) return rc;
     cudaEventElapsedTime(&m->last_step_ms, m->ev_begin, m->ev_end);

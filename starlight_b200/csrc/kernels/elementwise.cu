@@ -22,6 +22,7 @@ thread_local bool t_pdl = true;
 bool pdl_enabled() { return t_pdl; }
 void set_pdl_enabled(bool on) { t_pdl = on; }
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+void add_launches(int64_t n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 namespace {
 

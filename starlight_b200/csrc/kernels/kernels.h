@@ -37,8 +37,10 @@ cudaError_t rope(cudaStream_t s, const float *x, const uint32_t *positions, floa
 // ---- layout.cu ---------------------------------------------------------------
 cudaError_t gather(cudaStream_t s, const float *table, const uint32_t *ids, float *out,
                    size_t vocab, size_t hidden, size_t rows, uint32_t *error_flag);
+// d_seq_len: device copy of seq_len (graph replay) or null; err: error word.
 cudaError_t last_token(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
-                       size_t hidden, size_t seq_len);
+                       size_t hidden, size_t seq_len, const uint32_t *d_seq_len = nullptr,
+                       uint32_t *err = nullptr);
 cudaError_t split_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
                         size_t heads, size_t head_dim);
 cudaError_t merge_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
@@ -120,6 +122,7 @@ cudaError_t fill_normal(cudaStream_t s, float *out, size_t n, uint64_t seed, uin
 // Launch counter (incremented by every launcher).
 uint64_t launch_count();
 void count_launch();
+void add_launches(int64_t n);  // graph replays (n > 0) and aborted captures (n < 0)
 
 }  // namespace k
 }  // namespace slc

@@ -21,6 +21,7 @@ struct RowMap {
     const uint32_t *ids;
     size_t vocab, batch, seq, heads, seq_len;
     uint32_t *error_flag;
+    const uint32_t *d_seq_len;  // LastToken: device copy of seq_len, or null
 };
 
 __device__ __forceinline__ bool source_row(const RowMap &m, size_t r, size_t *src) {
@@ -34,9 +35,15 @@ __device__ __forceinline__ bool source_row(const RowMap &m, size_t r, size_t *sr
         *src = id;
         return true;
     }
-    case kLastToken:  // out row b <- input row (b, seq_len - 1)
-        *src = r * m.seq + (m.seq_len - 1);
+    case kLastToken: {  // out row b <- input row (b, seq_len - 1)
+        const size_t seq_len = m.d_seq_len ? (size_t)*m.d_seq_len : m.seq_len;
+        if (seq_len < 1 || seq_len > m.seq) {  // validated on the host; guard anyway
+            report_error(m.error_flag, kErrBadScalar);
+            return false;
+        }
+        *src = r * m.seq + (seq_len - 1);
         return true;
+    }
     case kSplit: {  // out row (b, h, t) <- input row (b, t, h)
         size_t t = r % m.seq, bh = r / m.seq, h = bh % m.heads, b = bh / m.heads;
         *src = (b * m.seq + t) * m.heads + h;
@@ -94,25 +101,25 @@ cudaError_t launch(cudaStream_t s, const float *src, float *dst, size_t rows, si
 
 cudaError_t gather(cudaStream_t s, const float *table, const uint32_t *ids, float *out,
                    size_t vocab, size_t hidden, size_t rows, uint32_t *error_flag) {
-    RowMap m{kGather, ids, vocab, 0, 0, 0, 0, error_flag};
+    RowMap m{kGather, ids, vocab, 0, 0, 0, 0, error_flag, nullptr};
     return launch(s, table, out, rows, hidden, m);
 }
 
 cudaError_t last_token(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
-                       size_t hidden, size_t seq_len) {
-    RowMap m{kLastToken, nullptr, 0, batch, seq, 0, seq_len, nullptr};
+                       size_t hidden, size_t seq_len, const uint32_t *d_seq_len, uint32_t *err) {
+    RowMap m{kLastToken, nullptr, 0, batch, seq, 0, seq_len, err, d_seq_len};
     return launch(s, x, out, batch, hidden, m);
 }
 
 cudaError_t split_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
                         size_t heads, size_t head_dim) {
-    RowMap m{kSplit, nullptr, 0, batch, seq, heads, 0, nullptr};
+    RowMap m{kSplit, nullptr, 0, batch, seq, heads, 0, nullptr, nullptr};
     return launch(s, x, out, batch * seq * heads, head_dim, m);
 }
 
 cudaError_t merge_heads(cudaStream_t s, const float *x, float *out, size_t batch, size_t seq,
                         size_t heads, size_t head_dim) {
-    RowMap m{kMerge, nullptr, 0, batch, seq, heads, 0, nullptr};
+    RowMap m{kMerge, nullptr, 0, batch, seq, heads, 0, nullptr, nullptr};
     return launch(s, x, out, batch * seq * heads, head_dim, m);
 }
 

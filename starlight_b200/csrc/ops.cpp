@@ -434,7 +434,8 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
         REQUIRE(xp);
         if (seq_len < 1 || seq_len > sq) return ck.exec("last_token requires 1 <= seq_len <= seq");
         if (!launch) return SLC_OK;
-        return finish(ck, k::last_token(s, xp, ck.output(), b, sq, h, seq_len));
+        return finish(ck, k::last_token(s, xp, ck.output(), b, sq, h, seq_len, c.dyn_scalars,
+                                        d->device_flag));
     }
     case SLC_OP_KV_APPEND: {
         Dims kd, vd;
@@ -456,7 +457,7 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
         if (past + sq > max_seq) return ck.exec("past_len + seq exceeds max_seq");
         if (!launch) return SLC_OK;
         k::KvGeometry g{b, layers, layer, hkv, hd, max_seq};
-        return finish(ck, k::kv_append(s, kp, vp, ck.state(), g, past, sq));
+        return finish(ck, k::kv_append(s, kp, vp, ck.state(), g, past, sq, c.dyn_scalars));
     }
     case SLC_OP_SPLIT_HEADS: {
         Dims x, o;
@@ -656,8 +657,9 @@ Cmd make_cmd(const slc_op *op, const slc_buffer_ref *in, const slc_value *iv, ui
 int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
                        const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
                        const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
-                       uint64_t n_scalars) {
+                       uint64_t n_scalars, const uint32_t *dyn_scalars) {
     Cmd c = make_cmd(op, in, iv, n_in, out, ov, n_out, scalars, n_scalars);
+    c.dyn_scalars = dyn_scalars;
     return run_op(d, c, true);
 }
 

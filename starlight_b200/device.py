@@ -133,6 +133,11 @@ class _Caps(C.Structure):
                 ("quant_formats", C.c_uint32)]
 
 
+class _CaptureInfo(C.Structure):
+    _fields_ = [("captures", C.c_uint64), ("replays", C.c_uint64),
+                ("replayed_commands", C.c_uint64), ("eager_commands", C.c_uint64)]
+
+
 class _Options(C.Structure):
     _fields_ = [("workspace_bytes", C.c_uint64), ("staging_bytes", C.c_uint64)]
 
@@ -266,9 +271,12 @@ def load_library():
                                      C.c_uint32, C.c_uint32, _BufferRef]),
         "slc_copy_f32_from_device": (C.c_int, [P, C.c_uint32, C.c_uint64, P, C.c_uint64]),
         "slc_buffer_device_ptr": (C.c_int, [P, C.c_uint32, C.POINTER(P)]),
+        "slc_release": (C.c_int, [P, C.c_uint32]),
         "slc_device_stream": (C.c_int, [P, C.POINTER(P)]),
         "slc_kernel_launch_count": (C.c_uint64, [P]),
         "slc_set_capture": (C.c_int, [P, C.c_int]),
+        "slc_flush": (C.c_int, [P]),
+        "slc_capture_stats": (C.c_int, [P, C.POINTER(_CaptureInfo)]),
         "slc_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
         "slc_comm_init": (C.c_int, [P, C.POINTER(C.c_uint8), C.c_int, C.c_int]),
         "slc_comm_world": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
@@ -287,8 +295,9 @@ def exported_symbols():
             "slc_get_capabilities", "slc_status_name", "slc_allocate_f32", "slc_allocate_u32",
             "slc_upload_f32", "slc_upload_u32", "slc_download_f32", "slc_download_u32",
             "slc_dispatch", "slc_synchronize", "slc_bind_quant", "slc_quantize",
-            "slc_dequantize", "slc_copy_f32_from_device", "slc_buffer_device_ptr",
-            "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture",
+            "slc_dequantize", "slc_copy_f32_from_device", "slc_buffer_device_ptr", "slc_release",
+            "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture", "slc_flush",
+            "slc_capture_stats",
             "slc_comm_unique_id", "slc_comm_init", "slc_comm_world"]
 
 
@@ -406,6 +415,10 @@ class CudaDevice:
         self._check(self._lib.slc_copy_f32_from_device(self._d, buffer, offset,
                                                        C.c_void_p(device_ptr), length))
 
+    def release(self, buffer: int):
+        """Frees a buffer's device memory (its BufferId becomes invalid)."""
+        self._check(self._lib.slc_release(self._d, buffer))
+
     def device_ptr(self, buffer: int) -> int:
         p = C.c_void_p()
         self._check(self._lib.slc_buffer_device_ptr(self._d, buffer, C.byref(p)))
@@ -420,7 +433,17 @@ class CudaDevice:
         return int(self._lib.slc_kernel_launch_count(self._d))
 
     def set_capture(self, enabled: bool):
+        """Command capture and CUDA-graph replay (include/starlight_cuda.h)."""
         self._check(self._lib.slc_set_capture(self._d, 1 if enabled else 0))
+
+    def flush(self):
+        """Submits deferred (captured) work without waiting for it."""
+        self._check(self._lib.slc_flush(self._d))
+
+    def capture_stats(self) -> dict:
+        info = _CaptureInfo()
+        self._check(self._lib.slc_capture_stats(self._d, C.byref(info)))
+        return {f: int(getattr(info, f)) for f, _ in _CaptureInfo._fields_}
 
     def comm_init(self, unique_id: bytes, rank: int, world: int):
         buf = (C.c_uint8 * 128)(*unique_id)
