@@ -20,6 +20,32 @@ LAYER_ROLES = ROLES[1:10]
 PREFILL, DECODE = 0, 1
 
 
+# Tensor-parallel layout of every weight role (the engine's add_weight in
+# starlight_b200/csrc/engine.cpp): 0 replicated, 1 split by output rows
+# (q, k, v, gate, up, lm_head: column-parallel matmuls), 2 split by input
+# columns (o, down: row-parallel matmuls followed by an all-reduce).
+SHARDING = {"embed": 0, "attn_norm": 0, "q": 1, "k": 1, "v": 1, "o": 2, "mlp_norm": 0,
+            "gate": 1, "up": 1, "down": 2, "final_norm": 0, "lm_head": 1}
+
+
+def full_shape(cfg: "LlamaConfig", role: str) -> tuple:
+    """Unsharded [rows, cols] of a weight role."""
+    H, D = cfg.hidden, cfg.head_dim
+    return {"embed": (cfg.vocab, H), "attn_norm": (1, H), "q": (cfg.heads * D, H),
+            "k": (cfg.kv_heads * D, H), "v": (cfg.kv_heads * D, H), "o": (H, cfg.heads * D),
+            "mlp_norm": (1, H), "gate": (cfg.inter, H), "up": (cfg.inter, H),
+            "down": (H, cfg.inter), "final_norm": (1, H), "lm_head": (cfg.vocab, H)}[role]
+
+
+def shard_plan(cfg: "LlamaConfig", role: str, rank: int, world: int) -> tuple:
+    """(row0, rows, col0, cols) of `rank`'s shard of a weight role."""
+    fr, fc = full_shape(cfg, role)
+    kind = SHARDING[role]
+    rows = fr // world if kind == 1 else fr
+    cols = fc // world if kind == 2 else fc
+    return (rank * rows if kind == 1 else 0, rows, rank * cols if kind == 2 else 0, cols)
+
+
 class _Config(C.Structure):
     _fields_ = [("layers", C.c_uint32), ("hidden", C.c_uint32), ("heads", C.c_uint32),
                 ("kv_heads", C.c_uint32), ("head_dim", C.c_uint32), ("inter", C.c_uint32),
