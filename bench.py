@@ -54,6 +54,9 @@ def parse_args(argv=None):
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=32, help="(testing only) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv", type=str, default=None, metavar="N,K,M",
+                    help="profiling aid: only run one quantized MatMulNT shape (INT4 g128, "
+                         "random codes) --steps times and print its time")
     return ap.parse_args(argv)
 
 
@@ -67,11 +70,12 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic():
-    """DRAM bytes per launch of the GEMV from the committed ncu summary, if any."""
+def profile_traffic_ratio():
+    """DRAM bytes / algorithmic bytes of the GEMV, from the committed ncu
+    summary of one full-size launch (profiles/gemv_int4_decode_8b.md)."""
     try:
         for line in open(TRAFFIC_PROFILE):
-            if line.strip().startswith("traffic_bytes_per_launch:"):
+            if line.strip().startswith("traffic_ratio:"):
                 return float(line.split(":", 1)[1].strip().split()[0])
     except Exception:
         pass
@@ -327,7 +331,10 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
         b = algo_bytes(subset[0][1])
         shapes[key] = {"launch_us": round(us, 2), "gbs": round(b / us / 1e3, 1),
                        "frac": round(b / us / 1e3 / peak[0], 3), "launches": len(subset)}
-    traffic = profile_traffic()
+    # ncu traffic of one full-size launch, scaled to this mix's average launch
+    # (traffic grows with the bytes streamed: each weight byte is read once).
+    ratio = profile_traffic_ratio()
+    traffic = ratio * per_launch_bytes if ratio is not None else None
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0], "traffic": traffic,
             "kernel": "qgemv_tma<INT4> (MatMulNT, M=%d) over one decode step's weight mix" % batch,
@@ -471,8 +478,56 @@ def run_ours(args, dist: Dist):
     return result
 
 
+def run_gemv_only(args):
+    """One quantized MatMulNT shape, `--steps` launches after `--warmup`, on
+    16 distinct weight matrices in turn (so that the launches read HBM, not
+    L2): a small, self-contained case for kernel profiles."""
+    import torch
+    from starlight_b200.device import BufferRef, CudaDevice, Op, OpCode, QuantFormat, Value
+    n, k, m = (int(v) for v in args.gemv.split(","))
+    dev = CudaDevice(0)
+    rng = np.random.default_rng(0)
+    words = n * (k // 2) // 4
+    mats = []
+    for i in range(16):
+        cb = dev.allocate_u32(words)
+        dev.upload_u32(cb, rng.integers(0, 2**32, size=words, dtype=np.uint64).astype(np.uint32))
+        sb = dev.allocate_f32(n * (k // 128))
+        dev.upload_f32(sb, (rng.random(n * (k // 128), dtype=np.float32) * 0.01))
+        dev.bind_quant(cb, sb, QuantFormat.Int4, 128)
+        mats.append(cb)
+    xb = dev.allocate_f32(m * k)
+    dev.upload_f32(xb, rng.standard_normal(m * k, dtype=np.float32))
+    ob = dev.allocate_f32(m * n)
+    stream = torch.cuda.ExternalStream(dev.stream())
+
+    def one(i):
+        dev.dispatch(Op(OpCode.MatMulNT), [BufferRef(xb, 0, m * k), BufferRef(mats[i % 16], 0, words)],
+                     [Value.f32((m, k)), Value.quantized((n, k), QuantFormat.Int4, 128)],
+                     [BufferRef(ob, 0, m * n)], [Value.f32((m, n))])
+
+    for i in range(args.warmup):
+        one(i)
+    dev.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        one(i)
+    t1.record(stream)
+    dev.synchronize()
+    t1.synchronize()
+    us = t0.elapsed_time(t1) * 1e3 / max(1, args.steps)
+    algo = n * k // 2 + 4 * n * (k // 128) + 4 * m * (k + n)
+    emit({"gemv": [n, k, m], "launch_us": us, "algorithmic_bytes": algo,
+          "gbs": algo / us / 1e3, "note": "stream launches from Python; host-bound below ~20 us"})
+    dev.close()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
+    if args.gemv:
+        return run_gemv_only(args)
     dist = Dist(args.gpus)
     try:
         if args.impl == "reference":

@@ -277,7 +277,7 @@ constexpr int kDecThreads = 128;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecMaxGroup = 8;
 constexpr int kDecKeysPerWarp = 4;  // keys in flight per warp
-constexpr int kDecMaxChunks = 512;  // chunks per (batch, kv_head)
+constexpr int kDecMaxChunks = 256;  // chunks per (batch, kv_head)
 
 struct DecodeParams {
     const float *q;        // [B, H, 1, D]
@@ -496,26 +496,36 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     // memory (the chunk statistics are loaded in parallel), then every
     // (row, dim) output adds the live chunks in ascending order.
     __shared__ float sm_w[kDecMaxGroup][kDecMaxChunks];
+    __shared__ float sm_l[kDecMaxGroup][kDecMaxChunks];
     __shared__ float sm_inv[kDecMaxGroup];
     const int live = min(p.chunks, (n_keys + p.chunk_keys - 1) / p.chunk_keys);
     const long long row0 = (long long)b * p.H + kvh * G;
+    // All chunk statistics in one parallel pass (independent loads) ...
     for (int i = threadIdx.x; i < G * live; i += kDecThreads) {
         const int r = i / live, c = i - r * live;
-        sm_w[r][c] = __ldcg(p.part_ml + ((row0 + r) * p.chunks + c) * 2);
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.part_ml) +
+                                 (row0 + r) * p.chunks + c);
+        sm_w[r][c] = ml.x;
+        sm_l[r][c] = ml.y;
     }
     __syncthreads();
-    if (threadIdx.x < G) {
-        const int r = threadIdx.x;
+    // ... then one warp per query row reduces them from shared memory.
+    for (int r = warp; r < G; r += kDecWarps) {
         float mm = -INFINITY;
-        for (int c = 0; c < live; c++) mm = fmaxf(mm, sm_w[r][c]);
-        float ll = 0.f;
-        for (int c = 0; c < live; c++) {
+        for (int c = lane; c < live; c += 32) mm = fmaxf(mm, sm_w[r][c]);
+        mm = warp_max(mm);
+        __syncwarp();
+        // Denominator in ascending chunk order (lane 0), weights in parallel.
+        for (int c = lane; c < live; c += 32) {
             const float mc = sm_w[r][c];
-            const float f = mc == -INFINITY ? 0.f : expf(mc - mm);
-            ll = fmaf(__ldcg(p.part_ml + ((row0 + r) * p.chunks + c) * 2 + 1), f, ll);
-            sm_w[r][c] = f;
+            sm_w[r][c] = mc == -INFINITY ? 0.f : expf(mc - mm);
         }
-        sm_inv[r] = ll;
+        __syncwarp();
+        if (lane == 0) {
+            float ll = 0.f;
+            for (int c = 0; c < live; c++) ll = fmaf(sm_l[r][c], sm_w[r][c], ll);
+            sm_inv[r] = ll;
+        }
     }
     __syncthreads();
     for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
