@@ -186,13 +186,59 @@ int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
     return 1;
 }
 
-// Runs the pending commands launch by launch; dyn = device table (capture).
+static bool overlaps(const slc_buffer_ref &a, const slc_buffer_ref &b) {
+    return a.buffer == b.buffer && a.offset < b.offset + b.len && b.offset < a.offset + a.len;
+}
+
+// Length of the run of MatMulNT commands starting at i that read the same
+// input with quantized weights and write pairwise disjoint outputs (which
+// then do not depend on each other): such a run can be one grouped launch.
+static int matmul_run(const std::vector<Rec> &v, size_t i) {
+    const Rec &a = v[i];
+    if (a.op.code != SLC_OP_MATMUL_NT || a.n_in != 2 || a.n_out != 1 ||
+        a.iv[1].encoding != SLC_ENC_GROUPWISE)
+        return 1;
+    size_t j = i + 1;
+    for (; j < v.size() && j - i < 4; j++) {
+        const Rec &b = v[j];
+        if (b.op.code != SLC_OP_MATMUL_NT || b.n_in != 2 || b.n_out != 1 ||
+            b.iv[1].encoding != SLC_ENC_GROUPWISE || memcmp(&b.in[0], &a.in[0], sizeof(a.in[0])) ||
+            memcmp(&b.iv[0], &a.iv[0], sizeof(a.iv[0])))
+            break;
+        bool clash = false;
+        for (size_t t = i; t < j; t++)
+            if (overlaps(v[t].out[0], b.out[0]) || overlaps(v[t].out[0], b.in[1]) ||
+                overlaps(b.out[0], a.in[0]))
+                clash = true;
+        if (clash) break;
+    }
+    return (int)(j - i);
+}
+
+// Runs the pending commands; dyn = kernels read the device scalar table
+// (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
-    for (const Rec &r : cs->pending) {
+    const std::vector<Rec> &v = cs->pending;
+    for (size_t i = 0; i < v.size();) {
+        const int run = matmul_run(v, i);
+        if (run > 1) {
+            MatmulMember mm[4];
+            for (int t = 0; t < run; t++)
+                mm[t] = MatmulMember{v[i + t].in, v[i + t].iv, v[i + t].out, v[i + t].ov};
+            bool launched = false;
+            int rc = slc_launch_matmul_group(d, mm, run, &launched);
+            if (rc != SLC_OK) return rc;
+            if (launched) {
+                i += run;
+                continue;
+            }
+        }
+        const Rec &r = v[i];
         const uint32_t *ds = (dyn && r.slot >= 0) ? cs->d_table + r.slot : nullptr;
         int rc = slc_launch_command(d, &r.op, r.in, r.iv, r.n_in, r.out, r.ov, r.n_out,
                                     r.scalars, r.n_scalars, ds);
         if (rc != SLC_OK) return rc;
+        i++;
     }
     return SLC_OK;
 }

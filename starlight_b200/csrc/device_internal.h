@@ -81,6 +81,16 @@ int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in
                        const slc_value *iv, uint64_t n_in, const slc_buffer_ref *out,
                        const slc_value *ov, uint64_t n_out, const uint32_t *scalars,
                        uint64_t n_scalars, const uint32_t *dyn_scalars);
+// Consecutive validated MatMulNT commands on the same input (quantized
+// weights, decode-sized): launched as one grouped GEMV when the TMA kernel
+// takes them (*launched = true); otherwise nothing is launched.
+struct MatmulMember {
+    const slc_buffer_ref *in;
+    const slc_value *iv;
+    const slc_buffer_ref *out;
+    const slc_value *ov;
+};
+int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched);
 // Try to record a validated command for graph replay. Returns 1 if the
 // command was recorded (launch deferred), 0 if it must be launched now.
 int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

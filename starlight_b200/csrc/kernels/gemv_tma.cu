@@ -77,26 +77,39 @@ constexpr int kMaxStages = 5;
 constexpr int kMinStages = 3;
 constexpr int kSmemLimit = 227 * 1024;
 
+constexpr int kMaxSeg = 4;  // weight matrices per launch (same x, same K)
+
 struct TmaArgs {
-    CUtensorMap codes_map;  // [N][row_bytes / 8] u64, box [128][32]
-    CUtensorMap scales_map; // [N][groups] f32, box [128][8]
+    CUtensorMap codes_map[kMaxSeg];   // [N][row_bytes / 8] u64, box [128][kRun * 8]
+    CUtensorMap scales_map[kMaxSeg];  // [N][groups] f32, box [128][8]
     const float *x;         // [M, K]
-    const uint8_t *codes;   // [N, row_bytes]
-    const float *scales;    // [N, groups]
-    float *out;             // [M, N]
-    float *partials;        // [slots, M, N]
+    const float *x2;        // SwiGLU: the staged activation is silu(x) * x2; else null
+    float *out[kMaxSeg];    // [M, N_s]
+    int N[kMaxSeg];         // rows of each matrix
+    int blk_end[kMaxSeg];   // cumulative 128-row block counts
+    int nseg;
+    float *partials;        // [slots][M][n_blocks * 128]
     unsigned *tickets;      // [n_blocks]
     uint32_t *err;          // device error word or null
-    int M, N, K, groups;
+    int M, K, groups;
     int gs_shift;           // log2(warp-steps per quantization group)
     long long row_bytes;
     long long spr;          // warp-steps per row
     long long total;        // n_blocks * spr
+    long long prow;         // n_blocks * 128: row stride of the partial slots
     int nstage;
     int S;                  // 16-byte units per staged activation column (padded)
     int ring_bytes;         // shared offset of the activation planes
     int unscale_floats;     // M * spr rounded up to an even count
 };
+
+// Matrix of a (global) block and the block's index inside it.
+__device__ __forceinline__ int block_segment(const TmaArgs &p, long long blk, int *local) {
+    int sgi = 0;
+    while (sgi + 1 < p.nseg && blk >= p.blk_end[sgi]) sgi++;
+    *local = (int)(blk - (sgi ? p.blk_end[sgi - 1] : 0));
+    return sgi;
+}
 
 template <int CW>
 __device__ __forceinline__ void consumer_sync() {
@@ -162,6 +175,27 @@ __device__ void stage_x(const TmaArgs &p, __half *xh, __half *xl, float *unscale
             const float2 q = __ldg(reinterpret_cast<const float2 *>(src));
             v[0] = q.x;
             v[1] = q.y;
+        }
+        if (p.x2) {
+            // SwiGLU: silu(gate) * up, the exact expression of the
+            // elementwise silu_mul kernel (so the product is bit-identical).
+            const float *src2 = p.x2 + (long long)col * p.K + k0;
+            float u[PER];
+            if constexpr (PER == 4) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(src2));
+                u[0] = q.x;
+                u[1] = q.y;
+                u[2] = q.z;
+                u[3] = q.w;
+            } else {
+                const float2 q = __ldg(reinterpret_cast<const float2 *>(src2));
+                u[0] = q.x;
+                u[1] = q.y;
+            }
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                v[i] = __fmul_rn(__fmul_rn(v[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])))),
+                                 u[i]);
         }
         float mx = 0.f;
 #pragma unroll
@@ -337,14 +371,18 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
         // warp-step step0) and one box of scales (128 rows x groups g4 ..
         // g4 + 7, g4 rounded down to 4 groups = 16 bytes).
         if (lane == 0) {
-            prefetch_tensormap(&p.codes_map);
-            prefetch_tensormap(&p.scales_map);
+            for (int i = 0; i < p.nseg; i++) {
+                prefetch_tensormap(&p.codes_map[i]);
+                prefetch_tensormap(&p.scales_map[i]);
+            }
             const uint64_t pol = policy_evict_first();
             int slot = 0, phase = 0;
             bool first_pass = true;
             for (long long u = u0; u < u1;) {
                 const long long blk = u / p.spr;
                 const long long run_end = min(u1, (blk + 1) * p.spr);
+                int lblk;
+                const int sgi = block_segment(p, blk, &lblk);
                 while (u < run_end) {
                     const int run = (int)min((long long)kRun, run_end - u);
                     if (!first_pass && !mbar_wait(&empty[slot], phase ^ 1, p.err, abort)) return;
@@ -352,9 +390,9 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
                     const int g4 = (int)(step0 >> p.gs_shift) & ~3;
                     unsigned char *sl = ring + slot * kSlotBytes;
                     mbar_arrive_expect_tx(&full[slot], (uint32_t)kSlotBytes);
-                    tma_load_2d(sl, &p.codes_map, (int)(step0 * (kStepBytes / 8)),
-                                (int)(blk * kBlockRows), &full[slot], pol);
-                    tma_load_2d(sl + kCodeBytes, &p.scales_map, g4, (int)(blk * kBlockRows),
+                    tma_load_2d(sl, &p.codes_map[sgi], (int)(step0 * (kStepBytes / 8)),
+                                lblk * kBlockRows, &full[slot], pol);
+                    tma_load_2d(sl + kCodeBytes, &p.scales_map[sgi], g4, lblk * kBlockRows,
                                 &full[slot], pol);
                     u += run;
                     if (++slot == p.nstage) {
@@ -376,8 +414,11 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     for (long long u = u0; u < u1;) {
         const long long blk = u / p.spr;
         const long long run_end = min(u1, (blk + 1) * p.spr);
-        const int row0 = (int)blk * kBlockRows + tile * kTileRows;
-        const bool active = row0 < p.N;
+        int lblk;
+        const int sgi = block_segment(p, blk, &lblk);
+        const int n_seg = p.N[sgi];
+        const int row0 = lblk * kBlockRows + tile * kTileRows;  // row in this matrix
+        const bool active = row0 < n_seg;
 #pragma unroll
         for (int jn = 0; jn < NT; jn++)
 #pragma unroll
@@ -431,18 +472,30 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
         const long long first = owner(blk * p.spr, p.total, grid);
         const long long last = owner((blk + 1) * p.spr - 1, p.total, grid);
         const int count = (int)(last - first + 1);
-        float *dst = count == 1 ? p.out : p.partials + (cta - first) * (long long)Mc * p.N;
+        // Direct output, or this CTA's partial slot (rows indexed over all
+        // matrices' blocks).
+        float *dst;
+        long long ld, r0;
+        if (count == 1) {
+            dst = p.out[sgi];
+            ld = n_seg;
+            r0 = row0;
+        } else {
+            dst = p.partials + (cta - first) * (long long)Mc * p.prow;
+            ld = p.prow;
+            r0 = blk * kBlockRows + tile * kTileRows;
+        }
         if (active && h == 0) {
 #pragma unroll
             for (int jn = 0; jn < NT; jn++) {
                 const int c0 = 2 * t + 8 * jn, c1 = c0 + 1;
                 if (c0 < Mc) {
-                    dst[(size_t)c0 * p.N + row0 + g] = res[jn][0];
-                    dst[(size_t)c0 * p.N + row0 + g + 8] = res[jn][2];
+                    dst[c0 * ld + r0 + g] = res[jn][0];
+                    dst[c0 * ld + r0 + g + 8] = res[jn][2];
                 }
                 if (c1 < Mc) {
-                    dst[(size_t)c1 * p.N + row0 + g] = res[jn][1];
-                    dst[(size_t)c1 * p.N + row0 + g + 8] = res[jn][3];
+                    dst[c1 * ld + r0 + g] = res[jn][1];
+                    dst[c1 * ld + r0 + g + 8] = res[jn][3];
                 }
             }
         }
@@ -458,15 +511,15 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
             consumer_sync<CW>();  // last_flag is rewritten by the next shared block
             if (is_last) {
                 __threadfence();
-                const int rows_here = min(kBlockRows, p.N - (int)blk * kBlockRows);
+                const int rows_here = min(kBlockRows, n_seg - lblk * kBlockRows);
                 for (int i = threadIdx.x; i < Mc * rows_here; i += CW * 32) {
-                    const int c = i / rows_here, r = (int)blk * kBlockRows + i % rows_here;
-                    const float *src = p.partials + (long long)c * p.N + r;
-                    const long long slot_stride = (long long)Mc * p.N;
+                    const int c = i / rows_here, r = i % rows_here;
+                    const float *src = p.partials + (long long)c * p.prow + blk * kBlockRows + r;
+                    const long long slot_stride = (long long)Mc * p.prow;
                     float v = 0.f;
 #pragma unroll 8
                     for (int sl = 0; sl < count; sl++) v += __ldcg(src + sl * slot_stride);
-                    p.out[(size_t)c * p.N + r] = v;
+                    p.out[sgi][(long long)c * n_seg + lblk * kBlockRows + r] = v;
                 }
                 if (threadIdx.x == 0) p.tickets[blk] = 0u;  // ready for the next launch
             }
@@ -477,7 +530,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
 struct TmaPlan {
     bool ok = false;
     int nstage = 0, S = 0, ring_bytes = 0, grid = 0, slots = 0, unscale_floats = 0;
-    long long spr = 0, total = 0;
+    long long spr = 0, total = 0, n_blocks = 0;
     size_t smem = 0;
 };
 
@@ -491,21 +544,33 @@ int padded_stride(int fmt, long long units) {
     return (int)S;
 }
 
-TmaPlan make_tma_plan(const QuantWeight &w, size_t m) {
-    TmaPlan pl;
+// One matrix the kernel can stream: shape, format and alignment rules.
+bool seg_ok(const QuantWeight &w) {
     const int kstep = w.format == 0 ? Fmt<0>::kStep : Fmt<1>::kStep;
-    if (m < 1 || m > 32 || w.n % kTileRows != 0 || w.k % w.group != 0 || w.group % kstep != 0 ||
-        w.row_bytes % kStepBytes != 0 || !aligned16(w.codes) || !aligned16(w.scales) ||
-        w.groups % 4 != 0 || w.n > (1u << 24) || w.k > (1u << 24) || w.k == 0)
-        return pl;
+    if (w.n == 0 || w.n % kTileRows != 0 || w.k == 0 || w.k % w.group != 0 ||
+        w.group % kstep != 0 || w.row_bytes % kStepBytes != 0 || !aligned16(w.codes) ||
+        !aligned16(w.scales) || w.groups % 4 != 0 || w.n > (1u << 24) || w.k > (1u << 24))
+        return false;
     const size_t gsteps = w.group / kstep;
-    if ((gsteps & (gsteps - 1)) != 0) return pl;  // power of two: shifts in the hot loop
-    pl.spr = (long long)(w.row_bytes / kStepBytes);
-    const long long n_blocks = (long long)((w.n + kBlockRows - 1) / kBlockRows);
+    return (gsteps & (gsteps - 1)) == 0;  // power of two: shifts in the hot loop
+}
+
+TmaPlan make_tma_plan(const QuantSeg *segs, int nseg, size_t m) {
+    TmaPlan pl;
+    if (nseg < 1 || nseg > kMaxSeg || m < 1 || m > 32) return pl;
+    const QuantWeight &w0 = segs[0].w;
+    long long n_blocks = 0;
+    for (int i = 0; i < nseg; i++) {
+        const QuantWeight &w = segs[i].w;
+        if (!seg_ok(w) || w.k != w0.k || w.format != w0.format || w.group != w0.group) return pl;
+        n_blocks += (long long)((w.n + kBlockRows - 1) / kBlockRows);
+    }
     if (n_blocks > 64 * 1024) return pl;
+    pl.n_blocks = n_blocks;
+    pl.spr = (long long)(w0.row_bytes / kStepBytes);
     pl.total = n_blocks * pl.spr;
     pl.grid = (int)std::min<long long>(pl.total, kSmCount);
-    pl.S = padded_stride(w.format, (long long)w.k / 8);
+    pl.S = padded_stride(w0.format, (long long)w0.k / 8);
     const size_t xbytes = (size_t)m * pl.S * 16 * 2;
     pl.unscale_floats = (int)(((long long)m * pl.spr + 1) / 2 * 2);
     const size_t fixed = (size_t)pl.unscale_floats * 4 + (size_t)kTiles * 32 * 16 * 4 +
@@ -565,19 +630,26 @@ bool tensor_maps(const QuantWeight &w, MapPair *out) {
 }
 
 template <int FMT, int NT, int SPLIT>
-cudaError_t launch_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
-                       const TmaPlan &pl, void *ws, uint32_t *err) {
+cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m,
+                       const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws,
+                       uint32_t *err) {
     TmaArgs a{};
-    MapPair maps;
-    if (!tensor_maps(w, &maps)) return cudaErrorInvalidValue;
-    a.codes_map = maps.codes;
-    a.scales_map = maps.scales;
+    long long blocks = 0;
+    for (int i = 0; i < nseg; i++) {
+        MapPair maps;
+        if (!tensor_maps(segs[i].w, &maps)) return cudaErrorInvalidValue;
+        a.codes_map[i] = maps.codes;
+        a.scales_map[i] = maps.scales;
+        a.out[i] = segs[i].out;
+        a.N[i] = (int)segs[i].w.n;
+        blocks += (long long)((segs[i].w.n + kBlockRows - 1) / kBlockRows);
+        a.blk_end[i] = (int)blocks;
+    }
+    const QuantWeight &w = segs[0].w;
+    a.nseg = nseg;
     a.x = x;
-    a.codes = w.codes;
-    a.scales = w.scales;
-    a.out = out;
+    a.x2 = x2;
     a.M = (int)m;
-    a.N = (int)w.n;
     a.K = (int)w.k;
     a.groups = (int)w.groups;
     a.gs_shift = 0;
@@ -585,6 +657,7 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, size_t m, const QuantWeig
     a.row_bytes = (long long)w.row_bytes;
     a.spr = pl.spr;
     a.total = pl.total;
+    a.prow = pl.n_blocks * kBlockRows;
     a.nstage = pl.nstage;
     a.S = pl.S;
     a.ring_bytes = pl.ring_bytes;
@@ -605,30 +678,49 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, size_t m, const QuantWeig
 
 }  // namespace
 
-size_t qgemv_tma_workspace_bytes(const QuantWeight &w, size_t m) {
-    TmaPlan pl = make_tma_plan(w, m);
-    if (!pl.ok) return (size_t)-1;
-    return 64 * 1024 * sizeof(unsigned) + (pl.slots > 1 ? (size_t)pl.slots * m * w.n * 4 : 0);
+bool qgemv_tma_group_supported(const QuantSeg *segs, int nseg, size_t m) {
+    return make_tma_plan(segs, nseg, m).ok;
 }
 
-bool qgemv_tma_supported(const QuantWeight &w, size_t m) { return make_tma_plan(w, m).ok; }
+size_t qgemv_tma_group_workspace_bytes(const QuantSeg *segs, int nseg, size_t m) {
+    TmaPlan pl = make_tma_plan(segs, nseg, m);
+    if (!pl.ok) return (size_t)-1;
+    return 64 * 1024 * sizeof(unsigned) +
+           (pl.slots > 1 ? (size_t)pl.slots * m * pl.n_blocks * kBlockRows * 4 : 0);
+}
+
+bool qgemv_tma_supported(const QuantWeight &w, size_t m) {
+    const QuantSeg seg{w, nullptr};
+    return qgemv_tma_group_supported(&seg, 1, m);
+}
+
+size_t qgemv_tma_workspace_bytes(const QuantWeight &w, size_t m) {
+    const QuantSeg seg{w, nullptr};
+    return qgemv_tma_group_workspace_bytes(&seg, 1, m);
+}
 
 bool qgemv_tma_x_aligned(const float *x) { return aligned16(x); }
 
-cudaError_t qgemv_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
-                      void *workspace, uint32_t *err) {
-    TmaPlan pl = make_tma_plan(w, m);
-    if (!pl.ok || !aligned16(x)) return cudaErrorInvalidValue;
+cudaError_t qgemv_tma_group(cudaStream_t s, const float *x, const float *x2, size_t m,
+                            const QuantSeg *segs, int nseg, void *workspace, uint32_t *err) {
+    TmaPlan pl = make_tma_plan(segs, nseg, m);
+    if (!pl.ok || !aligned16(x) || (x2 && !aligned16(x2))) return cudaErrorInvalidValue;
     const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
     // One column tile: two warps per 16-row tile (17 warps, 96 registers
     // each, no spills); more columns need the registers of one warp per tile.
-    if (w.format == 0)
-        return nt == 1 ? launch_tma<0, 1, 2>(s, x, m, w, out, pl, workspace, err)
-             : nt == 2 ? launch_tma<0, 2, 1>(s, x, m, w, out, pl, workspace, err)
-                       : launch_tma<0, 4, 1>(s, x, m, w, out, pl, workspace, err);
-    return nt == 1 ? launch_tma<1, 1, 2>(s, x, m, w, out, pl, workspace, err)
-         : nt == 2 ? launch_tma<1, 2, 1>(s, x, m, w, out, pl, workspace, err)
-                   : launch_tma<1, 4, 1>(s, x, m, w, out, pl, workspace, err);
+    if (segs[0].w.format == 0)
+        return nt == 1 ? launch_tma<0, 1, 2>(s, x, x2, m, segs, nseg, pl, workspace, err)
+             : nt == 2 ? launch_tma<0, 2, 1>(s, x, x2, m, segs, nseg, pl, workspace, err)
+                       : launch_tma<0, 4, 1>(s, x, x2, m, segs, nseg, pl, workspace, err);
+    return nt == 1 ? launch_tma<1, 1, 2>(s, x, x2, m, segs, nseg, pl, workspace, err)
+         : nt == 2 ? launch_tma<1, 2, 1>(s, x, x2, m, segs, nseg, pl, workspace, err)
+                   : launch_tma<1, 4, 1>(s, x, x2, m, segs, nseg, pl, workspace, err);
+}
+
+cudaError_t qgemv_tma(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                      void *workspace, uint32_t *err) {
+    const QuantSeg seg{w, out};
+    return qgemv_tma_group(s, x, nullptr, m, &seg, 1, workspace, err);
 }
 
 }  // namespace k

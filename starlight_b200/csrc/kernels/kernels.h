@@ -97,6 +97,17 @@ size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m);
 cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
                     void *workspace, size_t workspace_bytes, uint32_t *err = nullptr);
 // TMA-fed decode GEMV (gemv_tma.cu), small m; x must be 16-byte aligned.
+// A group is up to 4 matrices with the same input, K and format, streamed by
+// one launch; with x2 set the input is silu(x) * x2 (SwiGLU), computed while
+// it is staged.
+struct QuantSeg {
+    QuantWeight w;
+    float *out;  // [m, w.n]
+};
+bool qgemv_tma_group_supported(const QuantSeg *segs, int nseg, size_t m);
+size_t qgemv_tma_group_workspace_bytes(const QuantSeg *segs, int nseg, size_t m);
+cudaError_t qgemv_tma_group(cudaStream_t s, const float *x, const float *x2, size_t m,
+                            const QuantSeg *segs, int nseg, void *workspace, uint32_t *err);
 bool qgemv_tma_supported(const QuantWeight &w, size_t m);
 bool qgemv_tma_x_aligned(const float *x);
 size_t qgemv_tma_workspace_bytes(const QuantWeight &w, size_t m);

@@ -559,6 +559,25 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
         if (!launch || rows == 0) return SLC_OK;
         float *gb = intermediates(d), *ub = gb + chunk * inter;
         float *outp = ck.output();
+        // Decode-sized: gate and up in one TMA GEMV launch, then down with
+        // silu(gate) * up computed while its input is staged (two launches
+        // instead of four; the same arithmetic as the general path below).
+        if (wg.quant && wu.quant && wd.quant && rows <= 32 && rows <= chunk) {
+            const k::QuantSeg gu[2] = {{wg.q, gb}, {wu.q, ub}};
+            const k::QuantSeg dn[1] = {{wd.q, outp}};
+            if (k::qgemv_tma_group_supported(gu, 2, rows) &&
+                k::qgemv_tma_group_supported(dn, 1, rows) && k::qgemv_tma_x_aligned(xp) &&
+                k::qgemv_tma_x_aligned(gb) && k::qgemv_tma_x_aligned(ub) &&
+                k::qgemv_tma_group_workspace_bytes(gu, 2, rows) <= gemv_workspace_bytes(d) &&
+                k::qgemv_tma_group_workspace_bytes(dn, 1, rows) <= gemv_workspace_bytes(d)) {
+                cudaError_t e = k::qgemv_tma_group(s, xp, nullptr, rows, gu, 2, gemv_workspace(d),
+                                                   d->device_flag);
+                if (e == cudaSuccess)
+                    e = k::qgemv_tma_group(s, gb, ub, rows, dn, 1, gemv_workspace(d),
+                                           d->device_flag);
+                return finish(ck, e);
+            }
+        }
         for (uint64_t r0 = 0; r0 < rows; r0 += chunk) {
             uint64_t rc = std::min(chunk, rows - r0);
             cudaError_t e = matmul_rows(d, xp + r0 * hidden, rc, hidden, wg, inter, gb);
@@ -661,6 +680,46 @@ int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in
     Cmd c = make_cmd(op, in, iv, n_in, out, ov, n_out, scalars, n_scalars);
     c.dyn_scalars = dyn_scalars;
     return run_op(d, c, true);
+}
+
+int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched) {
+    *launched = false;
+    if (n < 2 || n > 4) return SLC_OK;
+    k::QuantSeg segs[4];
+    const float *x = nullptr;
+    uint64_t m = 0, kk = 0;
+    for (int i = 0; i < n; i++) {
+        const slc_value &xv = mm[i].iv[0], &wv = mm[i].iv[1], &ov = mm[i].ov[0];
+        if (wv.encoding != SLC_ENC_GROUPWISE || xv.rank < 2 || wv.rank != 2 || ov.rank < 2)
+            return SLC_OK;
+        uint64_t rows = 1;
+        for (uint32_t r = 0; r + 1 < xv.rank; r++) rows *= xv.dims[r];
+        const uint64_t k_i = xv.dims[xv.rank - 1];
+        const float *xp =
+            reinterpret_cast<const float *>(d->buffers[mm[i].in[0].buffer].ptr) + mm[i].in[0].offset;
+        if (i == 0) {
+            x = xp;
+            m = rows;
+            kk = k_i;
+        } else if (xp != x || rows != m || k_i != kk) {
+            return SLC_OK;
+        }
+        if (slc_quant_view(d, mm[i].in[1].buffer, mm[i].in[1].offset, wv.dims[0], kk,
+                           wv.quant_format, wv.group_size, &segs[i].w) != SLC_OK) {
+            d->last = slc_error{};
+            return SLC_OK;
+        }
+        segs[i].out =
+            reinterpret_cast<float *>(d->buffers[mm[i].out[0].buffer].ptr) + mm[i].out[0].offset;
+    }
+    if (m == 0 || m > 32 || !k::qgemv_tma_x_aligned(x) || !k::qgemv_tma_group_supported(segs, n, m) ||
+        k::qgemv_tma_group_workspace_bytes(segs, n, m) > gemv_workspace_bytes(d))
+        return SLC_OK;
+    cudaError_t e = k::qgemv_tma_group(d->stream, x, nullptr, m, segs, n, gemv_workspace(d),
+                                       d->device_flag);
+    if (e != cudaSuccess) return slc_fail(d, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
+    *launched = true;
+    return SLC_OK;
 }
 
 int slc_resolve_and_run(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

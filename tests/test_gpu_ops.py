@@ -453,6 +453,29 @@ def test_swiglu(dev, quant, rows, hidden, inter):
     assert_reduction(got, orc.swiglu(x, dense[0], dense[1], dense[2], rows, hidden, inter))
 
 
+@pytest.mark.parametrize("quant", [orc.INT4, orc.INT8])
+@pytest.mark.parametrize("rows,hidden,inter", [(1, 512, 1024), (3, 512, 1536), (8, 1024, 512),
+                                               (32, 512, 512)])
+def test_swiglu_decode_grouped_path(dev, quant, rows, hidden, inter):
+    # Group 128 and K a multiple of 512: gate and up in one TMA GEMV launch,
+    # down with silu(gate) * up computed while its input is staged.
+    lcg = Lcg(rows * 3 + hidden + inter)
+    x = lcg.fill(rows * hidden, -1, 1)
+    shapes = [(inter, hidden), (inter, hidden), (hidden, inter)]
+    qf = QuantFormat.Int4 if quant == orc.INT4 else QuantFormat.Int8
+    refs, vals, dense = [], [], []
+    for shp in shapes:
+        w = lcg.normal(shp[0] * shp[1], 0, 0.05)
+        codes, scales = orc.quantize(quant, w, shp[0], shp[1], 128)
+        cb, _, words = put_quant(dev, codes, scales, qf, 128)
+        refs.append(BufferRef(cb, 0, words))
+        vals.append(Value.quantized(shp, qf, 128))
+        dense.append(orc.dequantize(quant, codes, scales, shp[0], shp[1], 128))
+    got = run1(dev, Op(OpCode.SwiGlu), [put_f32(dev, x)] + refs, [F((rows, hidden))] + vals,
+               (rows, hidden))
+    assert_reduction(got, orc.swiglu(x, dense[0], dense[1], dense[2], rows, hidden, inter))
+
+
 @pytest.mark.parametrize("rows,hidden,nout", [(1, 1, 1), (3, 7, 5), (2, 33, 17), (4, 16, 9),
                                               (8, 4096, 256)])
 def test_rms_norm_matmul(dev, rows, hidden, nout):
