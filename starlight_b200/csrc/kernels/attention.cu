@@ -335,21 +335,22 @@ struct Vec<4> {
     __device__ static T zero() { return make_float4(0.f, 0.f, 0.f, 0.f); }
 };
 
-template <int VEC>
+// G: query heads per KV head; KPW: keys per warp loaded in one batch (all
+// of a 32-key chunk for G <= 4).
+template <int VEC, int G, int KPW>
 __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) {
     pdl_trigger();
     pdl_wait();
     using V = Vec<VEC>;
     using T = typename V::T;
     constexpr int D = 32 * VEC;
-    __shared__ float sm_o[kDecWarps][kDecMaxGroup][D];
-    __shared__ float sm_ml[kDecWarps][kDecMaxGroup][2];
+    __shared__ float sm_o[kDecWarps][G][D];
+    __shared__ float sm_ml[kDecWarps][G][2];
     __shared__ int is_last;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y, chunk = blockIdx.x;
     const int b = bh / p.Hkv, kvh = bh - b * p.Hkv;
-    const int G = p.G;
     int past = p.past;
     if (p.d_past) {
         past = (int)*p.d_past;
@@ -363,21 +364,18 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     const int k1 = min(n_keys, k0 + p.chunk_keys);
 
     // Query rows of the group (lane slice), pre-scaled.
-    T q[kDecMaxGroup];
+    T q[G];
 #pragma unroll
-    for (int r = 0; r < kDecMaxGroup; r++) {
-        q[r] = V::zero();
-        if (r < G) {
-            const float *qr = p.q + ((long long)(b * p.H + kvh * G + r)) * D + lane * VEC;
-            q[r] = V::ld(qr);
+    for (int r = 0; r < G; r++) {
+        const float *qr = p.q + ((long long)(b * p.H + kvh * G + r)) * D + lane * VEC;
+        q[r] = V::ld(qr);
 #pragma unroll
-            for (int i = 0; i < VEC; i++) V::set(q[r], i, V::get(q[r], i) * p.scale);
-        }
+        for (int i = 0; i < VEC; i++) V::set(q[r], i, V::get(q[r], i) * p.scale);
     }
-    float m[kDecMaxGroup], l[kDecMaxGroup];
-    T o[kDecMaxGroup];
+    float m[G], l[G];
+    T o[G];
 #pragma unroll
-    for (int r = 0; r < kDecMaxGroup; r++) {
+    for (int r = 0; r < G; r++) {
         m[r] = -INFINITY;
         l[r] = 0.f;
         o[r] = V::zero();
@@ -386,11 +384,12 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     const float *kbase = p.cache + b * p.batch_stride + p.layer_off + (long long)kvh * D + lane * VEC;
     const float *knew = p.k_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
     const float *vnew = p.v_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
-    for (int j0 = k0 + warp; j0 < k1; j0 += kDecWarps * kDecKeysPerWarp) {
-        T kv[kDecKeysPerWarp], vv[kDecKeysPerWarp];
+    for (int j0 = k0 + warp; j0 < k1; j0 += kDecWarps * KPW) {
+        // All of this warp's keys of the round in flight at once.
+        T kv[KPW], vv[KPW];
         int nk = 0;
 #pragma unroll
-        for (int i = 0; i < kDecKeysPerWarp; i++) {
+        for (int i = 0; i < KPW; i++) {
             const int j = j0 + i * kDecWarps;
             kv[i] = V::zero();
             vv[i] = V::zero();
@@ -411,48 +410,41 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
                 }
             }
         }
-        // Scores of this warp's keys for every query row.
-        float sc[kDecKeysPerWarp][kDecMaxGroup];
 #pragma unroll
-        for (int i = 0; i < kDecKeysPerWarp; i++)
+        for (int r = 0; r < G; r++) {
+            float sc[KPW];
+            float mb = -INFINITY;
 #pragma unroll
-            for (int r = 0; r < kDecMaxGroup; r++)
-                sc[i][r] = (r < G && i < nk) ? warp_sum(V::dot(q[r], kv[i])) : -INFINITY;
-#pragma unroll
-        for (int r = 0; r < kDecMaxGroup; r++) {
-            if (r < G) {
-                float mb = sc[0][r];
-#pragma unroll
-                for (int i = 1; i < kDecKeysPerWarp; i++) mb = fmaxf(mb, sc[i][r]);
-                const float m_new = fmaxf(m[r], mb);
-                const float alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new);
-                float lsum = l[r] * alpha;
-                T acc = o[r];
-#pragma unroll
-                for (int i = 0; i < VEC; i++) V::set(acc, i, V::get(acc, i) * alpha);
-#pragma unroll
-                for (int i = 0; i < kDecKeysPerWarp; i++) {
-                    const float pj = sc[i][r] == -INFINITY ? 0.f : expf(sc[i][r] - m_new);
-                    lsum += pj;
-                    V::axpby(acc, 1.0f, pj, vv[i]);
-                }
-                o[r] = acc;
-                l[r] = lsum;
-                m[r] = m_new;
+            for (int i = 0; i < KPW; i++) {
+                sc[i] = i < nk ? warp_sum(V::dot(q[r], kv[i])) : -INFINITY;
+                mb = fmaxf(mb, sc[i]);
             }
+            const float m_new = fmaxf(m[r], mb);
+            const float alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new);
+            float lsum = l[r] * alpha;
+            T acc = o[r];
+#pragma unroll
+            for (int i = 0; i < VEC; i++) V::set(acc, i, V::get(acc, i) * alpha);
+#pragma unroll
+            for (int i = 0; i < KPW; i++) {
+                const float pj = sc[i] == -INFINITY ? 0.f : expf(sc[i] - m_new);
+                lsum += pj;
+                V::axpby(acc, 1.0f, pj, vv[i]);
+            }
+            o[r] = acc;
+            l[r] = lsum;
+            m[r] = m_new;
         }
     }
 
     // Merge the warps (ascending warp order) into the CTA's partial.
 #pragma unroll
-    for (int r = 0; r < kDecMaxGroup; r++) {
-        if (r < G) {
+    for (int r = 0; r < G; r++) {
 #pragma unroll
-            for (int i = 0; i < VEC; i++) sm_o[warp][r][lane * VEC + i] = V::get(o[r], i);
-            if (lane == 0) {
-                sm_ml[warp][r][0] = m[r];
-                sm_ml[warp][r][1] = l[r];
-            }
+        for (int i = 0; i < VEC; i++) sm_o[warp][r][lane * VEC + i] = V::get(o[r], i);
+        if (lane == 0) {
+            sm_ml[warp][r][0] = m[r];
+            sm_ml[warp][r][1] = l[r];
         }
     }
     __syncthreads();
@@ -492,15 +484,14 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    // Chunk weights exp(m_c - M) / L per query row, computed once in shared
-    // memory (the chunk statistics are loaded in parallel), then every
-    // (row, dim) output adds the live chunks in ascending order.
-    __shared__ float sm_w[kDecMaxGroup][kDecMaxChunks];
-    __shared__ float sm_l[kDecMaxGroup][kDecMaxChunks];
-    __shared__ float sm_inv[kDecMaxGroup];
+    // Chunk weights exp(m_c - M) per query row from statistics loaded in one
+    // parallel pass; then every (row, dim) output adds the live chunks in
+    // ascending order, its partial values loaded before the sum.
+    __shared__ float sm_w[G][kDecMaxChunks];
+    __shared__ float sm_l[G][kDecMaxChunks];
+    __shared__ float sm_inv[G];
     const int live = min(p.chunks, (n_keys + p.chunk_keys - 1) / p.chunk_keys);
     const long long row0 = (long long)b * p.H + kvh * G;
-    // All chunk statistics in one parallel pass (independent loads) ...
     for (int i = threadIdx.x; i < G * live; i += kDecThreads) {
         const int r = i / live, c = i - r * live;
         const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.part_ml) +
@@ -509,13 +500,11 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         sm_l[r][c] = ml.y;
     }
     __syncthreads();
-    // ... then one warp per query row reduces them from shared memory.
     for (int r = warp; r < G; r += kDecWarps) {
         float mm = -INFINITY;
         for (int c = lane; c < live; c += 32) mm = fmaxf(mm, sm_w[r][c]);
         mm = warp_max(mm);
         __syncwarp();
-        // Denominator in ascending chunk order (lane 0), weights in parallel.
         for (int c = lane; c < live; c += 32) {
             const float mc = sm_w[r][c];
             sm_w[r][c] = mc == -INFINITY ? 0.f : expf(mc - mm);
@@ -528,13 +517,38 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         }
     }
     __syncthreads();
-    for (int idx = threadIdx.x; idx < G * D; idx += kDecThreads) {
-        const int r = idx / D, d = idx - r * D;
-        const float *po = p.part_o + (row0 + r) * p.chunks * D + d;
-        float acc = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < live; c++) acc = fmaf(__ldcg(po + (long long)c * D), sm_w[r][c], acc);
-        p.out[(row0 + r) * D + d] = __fdiv_rn(acc, sm_inv[r]);
+    constexpr int kOut = (G * D + kDecThreads - 1) / kDecThreads;  // outputs per thread
+    constexpr int kBatch = 8;                                      // chunks per load batch
+    float acc[kOut];
+#pragma unroll
+    for (int j = 0; j < kOut; j++) acc[j] = 0.f;
+    for (int c0 = 0; c0 < live; c0 += kBatch) {
+        float v[kBatch][kOut];
+#pragma unroll
+        for (int cc = 0; cc < kBatch; cc++)
+#pragma unroll
+            for (int j = 0; j < kOut; j++) {
+                const int idx = threadIdx.x + j * kDecThreads, c = c0 + cc;
+                const int r = idx / D, d = idx - r * D;
+                v[cc][j] = (idx < G * D && c < live)
+                               ? __ldcg(p.part_o + ((row0 + r) * p.chunks + c) * D + d)
+                               : 0.f;
+            }
+#pragma unroll
+        for (int cc = 0; cc < kBatch; cc++)
+#pragma unroll
+            for (int j = 0; j < kOut; j++) {
+                const int idx = threadIdx.x + j * kDecThreads, c = c0 + cc;
+                if (idx < G * D && c < live) acc[j] = fmaf(v[cc][j], sm_w[idx / D][c], acc[j]);
+            }
+    }
+#pragma unroll
+    for (int j = 0; j < kOut; j++) {
+        const int idx = threadIdx.x + j * kDecThreads;
+        if (idx < G * D) {
+            const int r = idx / D, d = idx - r * D;
+            p.out[(row0 + r) * D + d] = __fdiv_rn(acc[j], sm_inv[r]);
+        }
     }
     if (threadIdx.x == 0) p.tickets[bh] = 0u;  // ready for the next launch
 }
@@ -551,7 +565,9 @@ DecodePlan plan_decode(size_t batch, size_t kv_heads, size_t heads, size_t seq, 
     DecodePlan pl;
     if (seq != 1 || kv_heads == 0 || heads % kv_heads != 0) return pl;
     const size_t group = heads / kv_heads;
-    if (group > (size_t)kDecMaxGroup || (head_dim != 64 && head_dim != 128)) return pl;
+    if ((group != 1 && group != 2 && group != 4 && group != 8) ||
+        (head_dim != 64 && head_dim != 128))
+        return pl;
     if (keys_max > (size_t)INT32_MAX || batch * kv_heads > 65535) return pl;
     const size_t bh = batch * kv_heads;
     // About two CTAs per SM, each at least 32 keys.
@@ -634,10 +650,25 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
         p.chunks = dp.chunks;
         p.scale = scale;
         dim3 grid((unsigned)dp.chunks, (unsigned)(g.batch * g.kv_heads));
-        if (g.head_dim == 128)
-            launch_k(attention_decode<4>, grid, kDecThreads, 0, s, p);
-        else
-            launch_k(attention_decode<2>, grid, kDecThreads, 0, s, p);
+        const bool d128 = g.head_dim == 128;
+        switch (p.G) {
+        case 1:
+            launch_k(d128 ? attention_decode<4, 1, 8> : attention_decode<2, 1, 8>, grid,
+                     kDecThreads, 0, s, p);
+            break;
+        case 2:
+            launch_k(d128 ? attention_decode<4, 2, 8> : attention_decode<2, 2, 8>, grid,
+                     kDecThreads, 0, s, p);
+            break;
+        case 4:
+            launch_k(d128 ? attention_decode<4, 4, 8> : attention_decode<2, 4, 8>, grid,
+                     kDecThreads, 0, s, p);
+            break;
+        default:
+            launch_k(d128 ? attention_decode<4, 8, 4> : attention_decode<2, 8, 4>, grid,
+                     kDecThreads, 0, s, p);
+            break;
+        }
         count_launch();
         return cudaGetLastError();
     }
