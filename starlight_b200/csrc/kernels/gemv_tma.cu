@@ -96,6 +96,8 @@ struct TmaArgs {
     long long row_bytes;
     long long spr;          // warp-steps per row
     long long total;        // n_blocks * spr
+    long long units;        // n_blocks * split: the work units CTAs are given
+    int split;              // K slices per block (1: every CTA owns whole blocks)
     long long prow;         // n_blocks * 128: row stride of the partial slots
     int nstage;
     int S;                  // 16-byte units per staged activation column (padded)
@@ -116,9 +118,23 @@ __device__ __forceinline__ void consumer_sync() {
     asm volatile("bar.sync 1, %0;" ::"r"(CW * 32) : "memory");
 }
 
-// CTA whose range contains unit u (ranges are [c * total / grid, ...)).
-__device__ __forceinline__ long long owner(long long u, long long total, long long grid) {
-    return ((u + 1) * grid - 1) / total;
+// Work split. A unit is one K slice of one 128-row block: slice r of a block
+// covers warp-steps [r * spr / split, (r + 1) * spr / split). CTA c gets
+// units [c * units / grid, (c + 1) * units / grid), so with split == 1 it
+// owns whole blocks and never shares one (no partial sums).
+__device__ __forceinline__ long long unit_start(const TmaArgs &p, long long i) {
+    if (i >= p.units) return p.total;
+    const long long blk = i / p.split;
+    const long long r = i - blk * p.split;
+    return blk * p.spr + (r * p.spr) / p.split;
+}
+
+// CTA whose range contains warp-step u.
+__device__ __forceinline__ long long owner(const TmaArgs &p, long long u, long long grid) {
+    const long long blk = u / p.spr, st = u - blk * p.spr;
+    const long long r = (st * p.split + p.split - 1) / p.spr;  // slice holding step st
+    const long long i = blk * p.split + r;
+    return ((i + 1) * grid - 1) / p.units;
 }
 
 __device__ __forceinline__ int prescale_exponent(float mx) {
@@ -350,7 +366,8 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     volatile int *abort = last_flag + 1;  // set when a wait timed out
 
     const long long grid = gridDim.x, cta = blockIdx.x;
-    const long long u0 = cta * p.total / grid, u1 = (cta + 1) * p.total / grid;
+    const long long u0 = unit_start(p, cta * p.units / grid);
+    const long long u1 = unit_start(p, (cta + 1) * p.units / grid);
 
     // The producer streams weights before the previous kernel has finished
     // (weights are written only by uploads and quantization, which complete
@@ -469,8 +486,8 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
             }
             consumer_sync<CW>();
         }
-        const long long first = owner(blk * p.spr, p.total, grid);
-        const long long last = owner((blk + 1) * p.spr - 1, p.total, grid);
+        const long long first = owner(p, blk * p.spr, grid);
+        const long long last = owner(p, (blk + 1) * p.spr - 1, grid);
         const int count = (int)(last - first + 1);
         // Direct output, or this CTA's partial slot (rows indexed over all
         // matrices' blocks).
@@ -529,8 +546,8 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
 
 struct TmaPlan {
     bool ok = false;
-    int nstage = 0, S = 0, ring_bytes = 0, grid = 0, slots = 0, unscale_floats = 0;
-    long long spr = 0, total = 0, n_blocks = 0;
+    int nstage = 0, S = 0, ring_bytes = 0, grid = 0, slots = 0, unscale_floats = 0, split = 1;
+    long long spr = 0, total = 0, n_blocks = 0, units = 0;
     size_t smem = 0;
 };
 
@@ -569,7 +586,15 @@ TmaPlan make_tma_plan(const QuantSeg *segs, int nseg, size_t m) {
     pl.n_blocks = n_blocks;
     pl.spr = (long long)(w0.row_bytes / kStepBytes);
     pl.total = n_blocks * pl.spr;
-    pl.grid = (int)std::min<long long>(pl.total, kSmCount);
+    // One CTA consumes only ~20 GB/s (its dequant + MMA issue rate), so
+    // every matrix is spread over all SMs: units are single warp-steps and
+    // CTAs that share a block add partial sums. Whole blocks per CTA (no
+    // partial sums) only when they balance within 10% (e.g. a vocabulary
+    // projection of ~1000 blocks).
+    const long long per = (n_blocks + kSmCount - 1) / kSmCount;
+    pl.split = (n_blocks >= kSmCount && per * kSmCount * 10 <= n_blocks * 11) ? 1 : (int)pl.spr;
+    pl.units = n_blocks * pl.split;
+    pl.grid = (int)std::min<long long>(pl.units, kSmCount);
     pl.S = padded_stride(w0.format, (long long)w0.k / 8);
     const size_t xbytes = (size_t)m * pl.S * 16 * 2;
     pl.unscale_floats = (int)(((long long)m * pl.spr + 1) / 2 * 2);
@@ -581,9 +606,10 @@ TmaPlan make_tma_plan(const QuantSeg *segs, int nseg, size_t m) {
         if (pl.smem <= (size_t)kSmemLimit) break;
     }
     if (pl.nstage < kMinStages) return pl;
-    // Partial slots: the most CTAs that share one block (each CTA covers
-    // spr * n_blocks / grid warp-steps).
-    pl.slots = (int)std::min<long long>(pl.grid, (pl.grid + n_blocks - 1) / n_blocks + 1);
+    // Partial slots: the most CTAs that share one block.
+    pl.slots = pl.split == 1
+                   ? 1
+                   : (int)std::min<long long>(pl.grid, (pl.grid + n_blocks - 1) / n_blocks + 1);
     pl.ok = true;
     return pl;
 }
@@ -657,6 +683,8 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
     a.row_bytes = (long long)w.row_bytes;
     a.spr = pl.spr;
     a.total = pl.total;
+    a.units = pl.units;
+    a.split = pl.split;
     a.prow = pl.n_blocks * kBlockRows;
     a.nstage = pl.nstage;
     a.S = pl.S;
