@@ -41,6 +41,7 @@ sys.path.insert(0, ROOT)
 PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tok/s (Llama-3-8B-shaped llama-dense, INT4 g128)"
+METRIC_70B = "decode tok/s (Llama-2-70B-shaped llama-dense, INT8 g128)"
 TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemv_int4_decode_8b.md")
 
 
@@ -54,6 +55,14 @@ def parse_args(argv=None):
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--layers", type=int, default=32, help="(testing only) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--model", default="8b", choices=["8b", "70b"],
+                    help="8b: Llama-3-8B shape INT4 g128 (default workload); 70b: Llama-2-70B "
+                         "shape INT8 g128 (BASELINE configs[4])")
+    ap.add_argument("--synthetic-kv", action="store_true",
+                    help="fill the KV cache with N(0,1) values instead of running the prefill "
+                         "(decode cost does not depend on the cached values); default for 70b")
+    ap.add_argument("--sweep", action="store_true",
+                    help="per-operator and GEMV sweeps of BASELINE configs[1] and [2]")
     ap.add_argument("--gemv", type=str, default=None, metavar="N,K,M",
                     help="profiling aid: only run one quantized MatMulNT shape (INT4 g128, "
                          "random codes) --steps times and print its time")
@@ -288,25 +297,30 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
 
     def timed(segment):
         # With capture on, the third and later runs of the same segment are
-        # one CUDA-graph replay: the events then bracket device work only.
+        # one CUDA-graph replay. The segment is recorded (host work, nothing
+        # submitted) before the start event; the flush submits the replay, so
+        # the events bracket device work only.
         for _ in range(3):
             segment()
             dev.flush()
             dev.synchronize()
-        t0.record(stream)
+        total = 0.0
         for _ in range(reps):
             segment()
+            t0.record(stream)
             dev.flush()
-        t1.record(stream)
-        dev.synchronize()
-        t1.synchronize()
-        return t0.elapsed_time(t1)
+            t1.record(stream)
+            dev.synchronize()
+            t1.synchronize()
+            total += t0.elapsed_time(t1)
+        return total
 
     ms = timed(run_all)
 
     def algo_bytes(val):
         n, k = val.shape
-        return n * k // 2 + 4 * n * (k // 128) + 4 * batch * (k + n)
+        code_bytes = n * k // 2 if int(val.quant_format) == 0 else n * k
+        return code_bytes + 4 * n * (k // 128) + 4 * batch * (k + n)
 
     total_bytes = sum(algo_bytes(val) for _, val in launches)
     n_launch = len(launches)
@@ -337,7 +351,7 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
     traffic = ratio * per_launch_bytes if ratio is not None else None
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0], "traffic": traffic,
-            "kernel": "qgemv_tma<INT4> (MatMulNT, M=%d) over one decode step's weight mix" % batch,
+            "kernel": "qgemv_tma (quantized MatMulNT, M=%d) over one decode step's weight mix" % batch,
             "algorithmic_bytes_per_launch": per_launch_bytes, "launch_us": per_launch_s * 1e6,
             "peak_source": peak[1], "by_shape_NxK": shapes}
 
@@ -369,13 +383,14 @@ def rmsnorm_gbs(dev, peak):
     def segment():
         for i in range(reps):
             one(i)
-        dev.flush()
 
     for _ in range(3):  # eager, captured, replayed (with capture on)
         segment()
+        dev.flush()
         dev.synchronize()
+    segment()  # recorded only; the flush below submits the replay
     t0.record(stream)
-    segment()
+    dev.flush()
     t1.record(stream)
     dev.synchronize()
     t1.synchronize()
@@ -388,7 +403,7 @@ def rmsnorm_gbs(dev, peak):
 def run_ours(args, dist: Dist):
     import torch
     from starlight_b200.device import CudaDevice, comm_unique_id
-    from starlight_b200.engine import DECODE, PREFILL, LLAMA3_8B, Llama, LlamaConfig
+    from starlight_b200.engine import DECODE, PREFILL, LLAMA2_70B, LLAMA3_8B, Llama, LlamaConfig
 
     world, rank = dist.world, dist.rank
     torch.cuda.set_device(dist.local)
@@ -400,17 +415,29 @@ def run_ours(args, dist: Dist):
         uid = dist.broadcast_bytes(uid, 128)
         dev.comm_init(uid, rank, world)
     B, T = args.batch, args.prompt
+    base = LLAMA3_8B if args.model == "8b" else LLAMA2_70B
+    layers = base.layers if args.layers == 32 else args.layers
     max_seq = T + args.warmup + args.steps + 8
-    cfg = LlamaConfig(**{**LLAMA3_8B.__dict__, "batch": B, "prefill_len": T, "max_seq": max_seq,
-                         "layers": args.layers, "tp_rank": rank, "tp_world": world})
+    cfg = LlamaConfig(**{**base.__dict__, "batch": B, "prefill_len": T, "max_seq": max_seq,
+                         "layers": layers, "tp_rank": rank, "tp_world": world})
     model = Llama(dev, cfg)
     model.init_random(seed=8, std=0.02)
     V = cfg.vocab
     rng = np.random.default_rng(1234)
-    prompt = rng.integers(0, V, size=B * T, dtype=np.uint32)
-    pos = np.tile(np.arange(T, dtype=np.uint32), B)
-    logits = model.step(PREFILL, prompt, pos, T, 0)
-    ids = logits.argmax(axis=1).astype(np.uint32)
+    synthetic_kv = args.synthetic_kv or args.model == "70b"
+    if synthetic_kv:
+        # The decode step's cost does not depend on the cached keys/values:
+        # fill the cache instead of running the prefill (for 70B at batch 16 x
+        # 2048 tokens the prefill is ~4.5 PFLOP on the SIMT prefill path).
+        from starlight_b200.device import BufferRef
+        kb, kn = model.kv_buffer()
+        dev.fill_normal(BufferRef(kb, 0, kn), seed=99, mean=0.0, std=1.0)
+        ids = rng.integers(0, V, size=B, dtype=np.uint32)
+    else:
+        prompt = rng.integers(0, V, size=B * T, dtype=np.uint32)
+        pos = np.tile(np.arange(T, dtype=np.uint32), B)
+        logits = model.step(PREFILL, prompt, pos, T, 0)
+        ids = logits.argmax(axis=1).astype(np.uint32)
     past = T
     for _ in range(args.warmup):
         logits = model.step(DECODE, ids, np.full(B, past, np.uint32), 1, past)
@@ -449,12 +476,16 @@ def run_ours(args, dist: Dist):
         value = B * args.steps / (device_ms / 1e3)
         e2e = B * args.steps / wall
         result = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world,
+            "metric": METRIC if args.model == "8b" else METRIC_70B, "value": value, "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": device_ms / args.steps,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32 activations, int4 weights", "data": "synthetic",
-            "config": {"workload": "llama3-8b-int4-decode", "model": "llama-dense 8B shape",
-                       "batch": B, "prompt": T, "layers": cfg.layers, "quant": "int4 g128",
+            "dtype": "f32 activations, %s weights" % ("int4" if args.model == "8b" else "int8"),
+            "data": "synthetic" + (" (KV cache filled, no prefill)" if synthetic_kv else ""),
+            "config": {"workload": ("llama3-8b-int4-decode" if args.model == "8b"
+                                    else "llama2-70b-int8-decode"),
+                       "model": "llama-dense %s shape" % args.model.upper(),
+                       "batch": B, "prompt": T, "layers": cfg.layers,
+                       "quant": "int4 g128" if args.model == "8b" else "int8 g128",
                        "global_batch": B, "seq_len": T,
                        "parallelism": f"tp{world}" if world > 1 else "single",
                        "l2": "no flush: ~4 GB of weights streamed per step (> 126 MB L2)",
@@ -476,6 +507,156 @@ def run_ours(args, dist: Dist):
     model.close()
     dev.close()
     return result
+
+
+def run_sweep(args):
+    """BASELINE configs[1] and [2]: per-operator sweeps (RMSNorm, softmax,
+    SiLU, Mul, residual Add, RoPE at T in {1, 16, 256, 4096, 16384}) and the
+    quantized matmul sweep (decode GEMV at M in {1, 4, 16}, prefill at M in
+    {512, 2048}; INT4 and INT8, group 128). Every case is one captured
+    segment of launches over enough distinct input copies to exceed 2x L2,
+    timed as a CUDA-graph replay (device time only). Prints one JSON line."""
+    import torch
+    from starlight_b200.device import (BufferRef, CudaDevice, Op, OpCode, QuantFormat, Value,
+                                       ValueRole)
+    dev = CudaDevice(0)
+    dev.set_capture(True)
+    stream = torch.cuda.ExternalStream(dev.stream())
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    peak = hbm_peak()[0]
+    rng = np.random.default_rng(7)
+    L2x2 = 252 << 20
+
+    def timed(segment, reps=3):
+        # Third and later runs are graph replays; each is recorded on the host
+        # first and only its submission is bracketed by the events.
+        for _ in range(3):
+            segment()
+            dev.flush()
+            dev.synchronize()
+        total = 0.0
+        for _ in range(reps):
+            segment()
+            t0.record(stream)
+            dev.flush()
+            t1.record(stream)
+            dev.synchronize()
+            t1.synchronize()
+            total += t0.elapsed_time(t1)
+        return total / reps  # ms per segment
+
+    def f32buf(n, fill=None):
+        b = dev.allocate_f32(n)
+        if fill is not None:
+            dev.upload_f32(b, fill)
+        return b
+
+    ops = []
+    for T in (1, 16, 256, 4096, 16384):
+        cases = []
+        H = 4096
+        cases.append(("rms_norm", [T, H], 8 * T * H + 4 * H))
+        if T <= 4096:
+            cases.append(("softmax", [32 * T, 2048], 8 * 32 * T * 2048))
+        cases.append(("silu", [T, 14336], 8 * T * 14336))
+        cases.append(("mul", [T, 14336], 12 * T * 14336))
+        cases.append(("add", [T, H], 12 * T * H))
+        cases.append(("rope", [T, 32, 128], 8 * T * 4096 + 4 * T))
+        for name, shape, algo in cases:
+            n = int(np.prod(shape))
+            copies = max(1, min(16, -(-L2x2 // max(1, algo))))
+            data = rng.standard_normal(n, dtype=np.float32)
+            ins = [f32buf(n, data) for _ in range(copies)]
+            outs = [f32buf(n) for _ in range(2)]
+            extra = None
+            if name == "rms_norm":
+                extra = f32buf(H, (1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
+            elif name in ("mul", "add"):
+                extra = f32buf(n, rng.standard_normal(n, dtype=np.float32))
+            elif name == "rope":
+                extra = dev.allocate_u32(T)
+                dev.upload_u32(extra, np.arange(T, dtype=np.uint32))
+
+            def one(i, name=name, shape=shape, n=n, ins=ins, outs=outs, extra=extra):
+                x = BufferRef(ins[i % len(ins)], 0, n)
+                o = BufferRef(outs[i % 2], 0, n)
+                if name == "rms_norm":
+                    dev.dispatch(Op(OpCode.RmsNorm, eps=1e-5), [x, BufferRef(extra, 0, H)],
+                                 [Value.f32(shape), Value.f32((H,), ValueRole.Param)], [o],
+                                 [Value.f32(shape)])
+                elif name == "softmax":
+                    dev.dispatch(Op(OpCode.Softmax), [x], [Value.f32(shape)], [o], [Value.f32(shape)])
+                elif name == "silu":
+                    dev.dispatch(Op(OpCode.Silu), [x], [Value.f32(shape)], [o], [Value.f32(shape)])
+                elif name in ("mul", "add"):
+                    code = OpCode.Mul if name == "mul" else OpCode.Add
+                    dev.dispatch(Op(code), [x, BufferRef(extra, 0, n)],
+                                 [Value.f32(shape), Value.f32(shape)], [o], [Value.f32(shape)])
+                else:
+                    dev.dispatch(Op(OpCode.Rope, theta=500000.0), [x, BufferRef(extra, 0, T)],
+                                 [Value.f32((1, 32, T, 128)), Value.u32((1, T))], [o],
+                                 [Value.f32((1, 32, T, 128))])
+
+            reps_in = max(copies, 4)
+            ms = timed(lambda: [one(i) for i in range(reps_in)])
+            us = ms * 1e3 / reps_in
+            ops.append({"op": name, "shape": shape, "us": round(us, 2),
+                        "gbs": round(algo / us / 1e3, 1), "frac": round(algo / us / 1e3 / peak, 3)})
+            for b in ins + outs:
+                dev.release(b)
+            if extra is not None:
+                dev.release(extra)
+
+    gemv, prefill = [], []
+    for fmt in (QuantFormat.Int4, QuantFormat.Int8):
+        for k, n in ((4096, 4096), (4096, 14336), (14336, 4096), (4096, 128256)):
+            row_bytes = k // 2 if fmt == QuantFormat.Int4 else k
+            words = n * row_bytes // 4
+            wbytes = n * row_bytes + 4 * n * (k // 128)
+            copies = max(2, min(32, -(-L2x2 // wbytes)))
+            codes = rng.integers(0, 2**32, size=words, dtype=np.uint64).astype(np.uint32)
+            scales = (rng.random(n * (k // 128), dtype=np.float32) * 0.01).astype(np.float32)
+            mats = []
+            for _ in range(copies):
+                cb = dev.allocate_u32(words)
+                dev.upload_u32(cb, codes)
+                sb = f32buf(n * (k // 128), scales)
+                dev.bind_quant(cb, sb, fmt, 128)
+                mats.append((cb, sb))
+            for m in (1, 4, 16, 512, 2048):
+                if m >= 512 and k * n > 4096 * 14336:
+                    continue  # the vocabulary projection is not a prefill matmul per token block
+                xb = f32buf(m * k, rng.standard_normal(m * k, dtype=np.float32))
+                ob = f32buf(m * n)
+
+                def seg(m=m, xb=xb, ob=ob, mats=mats, k=k, n=n, words=words, fmt=fmt):
+                    for cb, _ in (mats if m < 512 else mats[:1]):
+                        dev.dispatch(Op(OpCode.MatMulNT),
+                                     [BufferRef(xb, 0, m * k), BufferRef(cb, 0, words)],
+                                     [Value.f32((m, k)), Value.quantized((n, k), fmt, 128)],
+                                     [BufferRef(ob, 0, m * n)], [Value.f32((m, n))])
+
+                launches = len(mats) if m < 512 else 1
+                us = timed(seg, reps=3 if m < 512 else 2) * 1e3 / launches
+                if m < 512:
+                    algo = wbytes + 4 * m * (k + n)
+                    gemv.append({"fmt": fmt.name, "K": k, "N": n, "M": m, "us": round(us, 2),
+                                 "gbs": round(algo / us / 1e3, 1),
+                                 "frac": round(algo / us / 1e3 / peak, 3)})
+                else:
+                    flop = 2.0 * m * n * k
+                    prefill.append({"fmt": fmt.name, "K": k, "N": n, "M": m, "us": round(us, 1),
+                                    "tflops": round(flop / us / 1e6, 2)})
+                dev.release(xb)
+                dev.release(ob)
+            for cb, sb in mats:
+                dev.release(cb)
+                dev.release(sb)
+    emit({"sweep": "configs[1] ops, configs[2] quantized matmul", "hbm_peak_gbs": peak,
+          "timing": "CUDA-graph replay of one captured segment; inputs rotated over >= 2x L2",
+          "ops": ops, "gemv": gemv, "prefill": prefill})
+    dev.close()
+    return 0
 
 
 def run_gemv_only(args):
@@ -528,6 +709,8 @@ def main(argv=None):
     args = parse_args(argv)
     if args.gemv:
         return run_gemv_only(args)
+    if args.sweep:
+        return run_sweep(args)
     dist = Dist(args.gpus)
     try:
         if args.impl == "reference":

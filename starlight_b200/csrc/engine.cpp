@@ -587,14 +587,19 @@ extern "C" int slc_llama_step(slc_llama *m, int mode, const uint32_t *ids,
     if (rc != SLC_OK) return rc;
     const uint32_t scalars_src[2] = {seq_len, past_len};
     uint32_t sc[4];
-    cudaEventRecord(m->ev_begin, d->stream);
+    // Device time of the step: with capture the dispatches below only record
+    // (the work is submitted by slc_flush), so the begin event goes after them
+    // and the events bracket device work only; host-side dispatch cost shows
+    // in the caller's wall clock.
+    const bool deferred = d->capture != nullptr;
+    if (!deferred) cudaEventRecord(m->ev_begin, d->stream);
     for (const Ready &r : p.ready) {
         for (size_t i = 0; i < r.scalar_src.size(); i++) sc[i] = scalars_src[r.scalar_src[i]];
         rc = slc_dispatch(d, &r.op, r.in.data(), r.iv.data(), r.in.size(), r.out.data(),
                           r.ov.data(), r.out.size(), sc, r.scalar_src.size());
         if (rc != SLC_OK) return rc;
     }
-    // Deferred (captured) work goes to the stream before the end event.
+    if (deferred) cudaEventRecord(m->ev_begin, d->stream);
     if ((rc = slc_flush(d)) != SLC_OK) return rc;
     cudaEventRecord(m->ev_end, d->stream);
     if ((rc = slc_synchronize(d)) != SLC_OK) return rc;

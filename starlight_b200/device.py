@@ -272,6 +272,8 @@ def load_library():
         "slc_copy_f32_from_device": (C.c_int, [P, C.c_uint32, C.c_uint64, P, C.c_uint64]),
         "slc_buffer_device_ptr": (C.c_int, [P, C.c_uint32, C.POINTER(P)]),
         "slc_release": (C.c_int, [P, C.c_uint32]),
+        "slc_fill_normal": (C.c_int, [P, _BufferRef, C.c_uint64, C.c_uint64, C.c_float,
+                                      C.c_float]),
         "slc_device_stream": (C.c_int, [P, C.POINTER(P)]),
         "slc_kernel_launch_count": (C.c_uint64, [P]),
         "slc_set_capture": (C.c_int, [P, C.c_int]),
@@ -296,6 +298,7 @@ def exported_symbols():
             "slc_upload_f32", "slc_upload_u32", "slc_download_f32", "slc_download_u32",
             "slc_dispatch", "slc_synchronize", "slc_bind_quant", "slc_quantize",
             "slc_dequantize", "slc_copy_f32_from_device", "slc_buffer_device_ptr", "slc_release",
+            "slc_fill_normal",
             "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture", "slc_flush",
             "slc_capture_stats",
             "slc_comm_unique_id", "slc_comm_init", "slc_comm_world"]
@@ -414,6 +417,12 @@ class CudaDevice:
     def copy_f32_from_device(self, buffer: int, offset: int, device_ptr: int, length: int):
         self._check(self._lib.slc_copy_f32_from_device(self._d, buffer, offset,
                                                        C.c_void_p(device_ptr), length))
+
+    def fill_normal(self, ref: BufferRef, seed: int, offset: int = 0, mean: float = 0.0,
+                    std: float = 1.0):
+        """Fills an F32 ref with N(mean, std) draws (synthetic data on the device)."""
+        self._check(self._lib.slc_fill_normal(self._d, _BufferRef(ref.buffer, 0, ref.offset, ref.len),
+                                              seed, offset, mean, std))
 
     def release(self, buffer: int):
         """Frees a buffer's device memory (its BufferId becomes invalid)."""
