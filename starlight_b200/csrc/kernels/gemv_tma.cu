@@ -103,6 +103,10 @@ struct TmaArgs {
     int S;                  // 16-byte units per staged activation column (padded)
     int ring_bytes;         // shared offset of the activation planes
     int unscale_floats;     // M * spr rounded up to an even count
+    // Integer consumer (qgemv_imma) only:
+    int Sn;                 // bytes per digit column (= 32 mod 128)
+    int ncol;               // digit columns: 3 * M
+    int xd_off, fx_off, red_off;  // shared offsets of digits, factors, block sums
 };
 
 // Matrix of a (global) block and the block's index inside it.
@@ -342,6 +346,45 @@ __device__ __forceinline__ void stage_math(const TmaArgs &p, const unsigned char
     }
 }
 
+// Producer (one thread): per stage one box of codes (128 rows x 320 bytes
+// from warp-step step0) and one box of scales (128 rows x groups g4 ..
+// g4 + 7, g4 rounded down to 4 groups = 16 bytes) into the next ring slot.
+__device__ __forceinline__ void produce(const TmaArgs &p, unsigned char *ring, uint64_t *full,
+                                        uint64_t *empty, volatile int *abort, long long u0,
+                                        long long u1) {
+    for (int i = 0; i < p.nseg; i++) {
+        prefetch_tensormap(&p.codes_map[i]);
+        prefetch_tensormap(&p.scales_map[i]);
+    }
+    const uint64_t pol = policy_evict_first();
+    int slot = 0, phase = 0;
+    bool first_pass = true;
+    for (long long u = u0; u < u1;) {
+        const long long blk = u / p.spr;
+        const long long run_end = min(u1, (blk + 1) * p.spr);
+        int lblk;
+        const int sgi = block_segment(p, blk, &lblk);
+        while (u < run_end) {
+            const int run = (int)min((long long)kRun, run_end - u);
+            if (!first_pass && !mbar_wait(&empty[slot], phase ^ 1, p.err, abort)) return;
+            const long long step0 = u - blk * p.spr;
+            const int g4 = (int)(step0 >> p.gs_shift) & ~3;
+            unsigned char *sl = ring + slot * kSlotBytes;
+            mbar_arrive_expect_tx(&full[slot], (uint32_t)kSlotBytes);
+            tma_load_2d(sl, &p.codes_map[sgi], (int)(step0 * (kStepBytes / 8)),
+                        lblk * kBlockRows, &full[slot], pol);
+            tma_load_2d(sl + kCodeBytes, &p.scales_map[sgi], g4, lblk * kBlockRows, &full[slot],
+                        pol);
+            u += run;
+            if (++slot == p.nstage) {
+                slot = 0;
+                phase ^= 1;
+                first_pass = false;
+            }
+        }
+    }
+}
+
 // SPLIT consumer warps share each 16-row tile (warp w: tile w % 8, steps
 // h = w / 8, h + SPLIT, ... of every stage); their sums meet in shared
 // memory at the end of a block's run.
@@ -384,42 +427,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     __syncthreads();
 
     if (warp == CW) {
-        // ---- producer: per stage one box of codes (128 rows x 256 bytes from
-        // warp-step step0) and one box of scales (128 rows x groups g4 ..
-        // g4 + 7, g4 rounded down to 4 groups = 16 bytes).
-        if (lane == 0) {
-            for (int i = 0; i < p.nseg; i++) {
-                prefetch_tensormap(&p.codes_map[i]);
-                prefetch_tensormap(&p.scales_map[i]);
-            }
-            const uint64_t pol = policy_evict_first();
-            int slot = 0, phase = 0;
-            bool first_pass = true;
-            for (long long u = u0; u < u1;) {
-                const long long blk = u / p.spr;
-                const long long run_end = min(u1, (blk + 1) * p.spr);
-                int lblk;
-                const int sgi = block_segment(p, blk, &lblk);
-                while (u < run_end) {
-                    const int run = (int)min((long long)kRun, run_end - u);
-                    if (!first_pass && !mbar_wait(&empty[slot], phase ^ 1, p.err, abort)) return;
-                    const long long step0 = u - blk * p.spr;
-                    const int g4 = (int)(step0 >> p.gs_shift) & ~3;
-                    unsigned char *sl = ring + slot * kSlotBytes;
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)kSlotBytes);
-                    tma_load_2d(sl, &p.codes_map[sgi], (int)(step0 * (kStepBytes / 8)),
-                                lblk * kBlockRows, &full[slot], pol);
-                    tma_load_2d(sl + kCodeBytes, &p.scales_map[sgi], g4, lblk * kBlockRows,
-                                &full[slot], pol);
-                    u += run;
-                    if (++slot == p.nstage) {
-                        slot = 0;
-                        phase ^= 1;
-                        first_pass = false;
-                    }
-                }
-            }
-        }
+        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1);
         return;
     }
 
@@ -544,12 +552,439 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Exact-integer consumer (qgemv_imma). The same producer, ring, work split and
+// partial-sum protocol as qgemv_tma, with the products formed by the s8 tensor
+// path (mma.sync m16n8k32, s8 x s8 -> s32) instead of f16:
+//
+//  * Codes become s8 without arithmetic: an INT4 nibble moved to the top of
+//    its byte is 16 x code (odd nibbles are masked in place, even nibbles
+//    shifted up by 4), INT8 bytes are used as they are.
+//  * Every activation block of one warp-step (128 k for INT4, 64 for INT8)
+//    of column m is written as x = 2^e * (d0 + d1 / 128 + d2 / 16384) with
+//    digits d in [-64, 64] (e from the block's largest magnitude, so that
+//    |x / 2^e| < 64): about 20 significant bits relative to the block's
+//    largest value, every step exact in f32.
+//  * The digits are the MMA's N dimension: column n = 3m + d, so one n8 tile
+//    carries the three digits of two activation columns and M = 1 or 2 costs
+//    4 (INT4) or 2 (INT8) MMAs per 16 rows x one warp-step.
+//  * Integer sums of one warp-step (|sum| < 2^21) convert to f32 exactly
+//    and are scaled by scale[n, group] * 2^e * 2^-7d (x 1/16 for INT4).
+// Column sums of the three digits are added at the end of a block.
+template <int FMT>
+struct Imma;
+template <>
+struct Imma<0> {
+    static constexpr int kWsBytes = 128;  // digit bytes per column per warp-step
+    static constexpr int kJ = 4;          // k32 MMAs per warp-step
+};
+template <>
+struct Imma<1> {
+    static constexpr int kWsBytes = 64;
+    static constexpr int kJ = 2;
+};
+
+// Byte of activation k (within its warp-step) inside the column's warp-step
+// block, laid out [j][t][8 bytes] so that lane (g, t) reads the B fragment
+// of MMA j with one 8-byte load: bytes 0..3 = register b0, 4..7 = b1.
+// INT4: lane quad t holds codes 32t .. 32t + 31; MMA j pairs the even
+// nibbles of word j (k = 32t + 8j + 2i) in b0 with the odd ones in b1.
+// INT8: lane quad t holds codes 16t .. 16t + 15; MMA j takes words 2j and
+// 2j + 1 (k = 16t + 8j + i and 16t + 8j + 4 + i).
+template <int FMT>
+__device__ __forceinline__ int imma_byte(int kl) {
+    if (FMT == 0) {
+        const int t = kl >> 5, j = (kl >> 3) & 3, i = (kl >> 1) & 3, odd = kl & 1;
+        return j * 32 + t * 8 + odd * 4 + i;
+    }
+    const int t = kl >> 4, j = (kl >> 3) & 1, h = (kl >> 2) & 1, i = kl & 3;
+    return j * 32 + t * 8 + h * 4 + i;
+}
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                       uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint2 lds64(const void *p) {
+    uint2 r;
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+
+// Exact int -> float for |c| < 2^22 on the integer and FP32 pipes.
+__device__ __forceinline__ float i2f_small(int c) {
+    return __int_as_float(c + 0x4B400000) - 12582912.0f;
+}
+
+// Stages all of x as digit planes (consumer warps only): block (m, ws) is
+// handled by one warp, each lane converting 4 (INT4) or 2 (INT8) values.
+template <int FMT, int CW, int NT>
+__device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx) {
+    constexpr int KSTEP = Fmt<FMT>::kStep;
+    constexpr int PER = KSTEP / 32;
+    constexpr int WSB = Imma<FMT>::kWsBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int spr = (int)p.spr;
+    const int blocks = p.M * spr;
+    for (int b = warp; b < blocks; b += CW) {
+        const int col = b / spr, st = b - col * spr;
+        const int k0 = st * KSTEP + lane * PER;
+        const float *src = p.x + (long long)col * p.K + k0;
+        float v[PER];
+        if constexpr (PER == 4) {
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(src));
+            v[0] = q.x;
+            v[1] = q.y;
+            v[2] = q.z;
+            v[3] = q.w;
+        } else {
+            const float2 q = __ldg(reinterpret_cast<const float2 *>(src));
+            v[0] = q.x;
+            v[1] = q.y;
+        }
+        if (p.x2) {
+            // SwiGLU: silu(gate) * up, the exact expression of the
+            // elementwise silu_mul kernel.
+            const float *src2 = p.x2 + (long long)col * p.K + k0;
+            float u[PER];
+            if constexpr (PER == 4) {
+                const float4 q = __ldg(reinterpret_cast<const float4 *>(src2));
+                u[0] = q.x;
+                u[1] = q.y;
+                u[2] = q.z;
+                u[3] = q.w;
+            } else {
+                const float2 q = __ldg(reinterpret_cast<const float2 *>(src2));
+                u[0] = q.x;
+                u[1] = q.y;
+            }
+#pragma unroll
+            for (int i = 0; i < PER; i++)
+                v[i] = __fmul_rn(__fmul_rn(v[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])))),
+                                 u[i]);
+        }
+        float mx = 0.f;
+        bool bad = false;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            const float a = fabsf(v[i]);
+            bad |= !(a <= 3.402823466e38f);  // inf or nan
+            mx = fmaxf(mx, a);
+        }
+        mx = warp_max(mx);
+        bad = __any_sync(0xffffffffu, bad);
+        int e = 0;
+        if (mx > 0.f && !bad) {
+            int ex;
+            frexpf(mx, &ex);
+            e = ex - 6;  // |x| < 2^ex, so |x / 2^e| < 64
+        }
+        int8_t *dst = xd + (3 * col) * p.Sn + st * WSB;
+#pragma unroll
+        for (int i = 0; i < PER; i++) {
+            float d0 = 0.f, d1 = 0.f, d2 = 0.f;
+            if (!bad) {
+                const float y = ldexpf(v[i], -e);
+                d0 = rintf(y);
+                float r = (y - d0) * 128.f;
+                d1 = rintf(r);
+                r = (r - d1) * 128.f;
+                d2 = rintf(r);
+            }
+            const int off = imma_byte<FMT>(lane * PER + i);
+            dst[off] = (int8_t)(int)d0;
+            dst[p.Sn + off] = (int8_t)(int)d1;
+            dst[2 * p.Sn + off] = (int8_t)(int)d2;
+        }
+        if (lane < 3) {
+            // 2^e, times 1/16 for the INT4 codes' byte position; non-finite
+            // input makes the column's outputs NaN.
+            float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
+            f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
+            fx[st * (8 * NT) + 3 * col + lane] = f;
+        }
+    }
+    // Padding columns 3M .. 8 NT - 1 contribute nothing.
+    const int pad = 8 * NT - 3 * p.M;
+    for (int i = threadIdx.x; i < spr * pad; i += CW * 32)
+        fx[(i / pad) * (8 * NT) + 3 * p.M + i % pad] = 0.f;
+    consumer_sync<CW>();
+}
+
+// One warp-step of one 16-row tile: integer sums c[nt] of the tile's rows
+// (g, g + 8) with the lane's digit columns (8 nt + 2t, + 1).
+template <int FMT, int NT>
+__device__ __forceinline__ void imma_step(const unsigned char *rowg, int pitch,
+                                          const unsigned char *xcell, int Sn, int ncol, int g,
+                                          int (&c)[NT][4]) {
+    constexpr int J = Imma<FMT>::kJ;
+    uint32_t ag[2 * J], a8[2 * J];  // per MMA j: (a0 | a2) of row g and (a1 | a3) of row g + 8
+    const uint4 wa = lds128(rowg);
+    const uint4 wb = lds128(rowg + 8 * pitch);
+    const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w}, qb[4] = {wb.x, wb.y, wb.z, wb.w};
+    if (FMT == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            ag[2 * j] = (qa[j] << 4) & 0xF0F0F0F0u;
+            ag[2 * j + 1] = qa[j] & 0xF0F0F0F0u;
+            a8[2 * j] = (qb[j] << 4) & 0xF0F0F0F0u;
+            a8[2 * j + 1] = qb[j] & 0xF0F0F0F0u;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            ag[j] = qa[j];
+            a8[j] = qb[j];
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) c[nt][i] = 0;
+        const int n = 8 * nt + g;
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            uint2 b = make_uint2(0u, 0u);
+            if (n < ncol) b = lds64(xcell + n * Sn + j * 32);
+            mma_s8(c[nt], ag[2 * j], a8[2 * j], ag[2 * j + 1], a8[2 * j + 1], b.x, b.y);
+        }
+    }
+}
+
+template <int FMT, int NT, int SPLIT, bool FULL>
+__device__ __forceinline__ void imma_stage(const TmaArgs &p, const unsigned char *base,
+                                           const float *ssl, int step0, int run, int h,
+                                           const unsigned char *xd, const float *fx, int g, int t,
+                                           float (&res)[NT][4]) {
+    constexpr int WSB = Imma<FMT>::kWsBytes;
+    const int g4 = (step0 >> p.gs_shift) & ~3;
+#pragma unroll
+    for (int jj = 0; jj < (kRun + SPLIT - 1) / SPLIT; jj++) {
+        const int j = jj * SPLIT + h;
+        if (j < kRun && (FULL || j < run)) {
+            int c[NT][4];
+            const int sw = step0 + j;
+            imma_step<FMT, NT>(base + j * kStepBytes, kPitch, xd + sw * WSB + t * 8, p.Sn,
+                               p.ncol, g, c);
+            const int gi = (sw >> p.gs_shift) - g4;
+            const float s0 = ssl[gi], s1 = ssl[8 * kScaleBox + gi];
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const float2 f = *reinterpret_cast<const float2 *>(fx + sw * (8 * NT) + 8 * nt + 2 * t);
+                res[nt][0] = fmaf(i2f_small(c[nt][0]), s0 * f.x, res[nt][0]);
+                res[nt][1] = fmaf(i2f_small(c[nt][1]), s0 * f.y, res[nt][1]);
+                res[nt][2] = fmaf(i2f_small(c[nt][2]), s1 * f.x, res[nt][2]);
+                res[nt][3] = fmaf(i2f_small(c[nt][3]), s1 * f.y, res[nt][3]);
+            }
+        }
+    }
+}
+
+template <int FMT, int NT, int SPLIT>
+__global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
+    qgemv_imma(const __grid_constant__ TmaArgs p) {
+    constexpr int CW = kTiles * SPLIT;  // consumer warps
+    constexpr int NC = 8 * NT;          // digit columns per lane tile row
+    extern __shared__ __align__(1024) unsigned char smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int tile = warp % kTiles, h = warp / kTiles;
+    const int Mc = p.M;
+
+    unsigned char *ring = smem;
+    int8_t *xd = reinterpret_cast<int8_t *>(smem + p.xd_off);
+    float *fx = reinterpret_cast<float *>(smem + p.fx_off);
+    float *red = reinterpret_cast<float *>(smem + p.red_off);  // [CW][16][NC]
+    uint64_t *full = reinterpret_cast<uint64_t *>(red + CW * 16 * NC);
+    uint64_t *empty = full + kMaxStages;
+    int *last_flag = reinterpret_cast<int *>(empty + kMaxStages);
+    volatile int *abort = last_flag + 1;
+
+    const long long grid = gridDim.x, cta = blockIdx.x;
+    const long long u0 = unit_start(p, cta * p.units / grid);
+    const long long u1 = unit_start(p, (cta + 1) * p.units / grid);
+
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < p.nstage; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], CW);
+        }
+        fence_mbar_init();
+        *abort = 0;
+    }
+    __syncthreads();
+
+    if (warp == CW) {
+        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1);
+        return;
+    }
+
+    pdl_wait();
+    stage_digits<FMT, CW, NT>(p, xd, fx);
+    float res[NT][4];
+    int slot = 0, phase = 0;
+    for (long long u = u0; u < u1;) {
+        const long long blk = u / p.spr;
+        const long long run_end = min(u1, (blk + 1) * p.spr);
+        int lblk;
+        const int sgi = block_segment(p, blk, &lblk);
+        const int n_seg = p.N[sgi];
+        const int row0 = lblk * kBlockRows + tile * kTileRows;
+        const bool active = row0 < n_seg;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) res[nt][i] = 0.f;
+        while (u < run_end) {
+            const int run = (int)min((long long)kRun, run_end - u);
+            const int step0 = (int)(u - blk * p.spr);
+            const bool ready = !*abort && mbar_wait(&full[slot], phase, p.err, abort);
+            if (ready && active) {
+                const unsigned char *sl = ring + slot * kSlotBytes;
+                const unsigned char *base = sl + (tile * kTileRows + g) * kPitch + t * 16;
+                const float *ssl = reinterpret_cast<const float *>(sl + kCodeBytes) +
+                                   (tile * kTileRows + g) * kScaleBox;
+                if (run == kRun)
+                    imma_stage<FMT, NT, SPLIT, true>(p, base, ssl, step0, run, h,
+                                                     reinterpret_cast<const unsigned char *>(xd),
+                                                     fx, g, t, res);
+                else
+                    imma_stage<FMT, NT, SPLIT, false>(p, base, ssl, step0, run, h,
+                                                      reinterpret_cast<const unsigned char *>(xd),
+                                                      fx, g, t, res);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+            u += run;
+            if (++slot == p.nstage) {
+                slot = 0;
+                phase ^= 1;
+            }
+        }
+
+        // ---- end of this CTA's run over the block: every warp's column
+        // sums meet in shared memory; output (m, row) = sum over the SPLIT
+        // warps of the tile, then over the three digit columns, in order.
+        float *rw = red + warp * 16 * NC;
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const int c0 = 8 * nt + 2 * t;
+            rw[g * NC + c0] = res[nt][0];
+            rw[g * NC + c0 + 1] = res[nt][1];
+            rw[(g + 8) * NC + c0] = res[nt][2];
+            rw[(g + 8) * NC + c0 + 1] = res[nt][3];
+        }
+        consumer_sync<CW>();
+        const long long first = owner(p, blk * p.spr, grid);
+        const long long last = owner(p, (blk + 1) * p.spr - 1, grid);
+        const int count = (int)(last - first + 1);
+        float *dst;
+        long long ld, rbase;
+        if (count == 1) {
+            dst = p.out[sgi];
+            ld = n_seg;
+            rbase = (long long)lblk * kBlockRows;
+        } else {
+            dst = p.partials + (cta - first) * (long long)Mc * p.prow;
+            ld = p.prow;
+            rbase = blk * kBlockRows;
+        }
+        for (int i = threadIdx.x; i < Mc * kBlockRows; i += CW * 32) {
+            const int m = i / kBlockRows, tr = i - m * kBlockRows;
+            const int tl = tr >> 4, r = tr & 15;
+            if (lblk * kBlockRows + tr >= n_seg) continue;
+            float v = 0.f;
+#pragma unroll
+            for (int hh = 0; hh < SPLIT; hh++) {
+                const float *q = red + ((hh * kTiles + tl) * 16 + r) * NC + 3 * m;
+                v += (q[0] + q[1]) + q[2];
+            }
+            dst[m * ld + rbase + tr] = v;
+        }
+        if (count > 1) {
+            __threadfence();
+            consumer_sync<CW>();
+            if (threadIdx.x == 0) {
+                const unsigned ticket = atomicAdd(&p.tickets[blk], 1u);
+                *last_flag = ticket == (unsigned)(count - 1);
+            }
+            consumer_sync<CW>();
+            const bool is_last = *last_flag;
+            if (is_last) {
+                __threadfence();
+                const int rows_here = min(kBlockRows, n_seg - lblk * kBlockRows);
+                for (int i = threadIdx.x; i < Mc * rows_here; i += CW * 32) {
+                    const int c = i / rows_here, r = i % rows_here;
+                    const float *src = p.partials + (long long)c * p.prow + blk * kBlockRows + r;
+                    const long long slot_stride = (long long)Mc * p.prow;
+                    float v = 0.f;
+#pragma unroll 8
+                    for (int sl = 0; sl < count; sl++) v += __ldcg(src + sl * slot_stride);
+                    p.out[sgi][(long long)c * n_seg + lblk * kBlockRows + r] = v;
+                }
+                if (threadIdx.x == 0) p.tickets[blk] = 0u;
+            }
+        }
+        // red and last_flag are rewritten for the next block.
+        consumer_sync<CW>();
+    }
+}
+
 struct TmaPlan {
     bool ok = false;
     int nstage = 0, S = 0, ring_bytes = 0, grid = 0, slots = 0, unscale_floats = 0, split = 1;
     long long spr = 0, total = 0, n_blocks = 0, units = 0;
     size_t smem = 0;
+    // Integer consumer (qgemv_imma), when its activation digits fit.
+    bool imma = false;
+    int int_nt = 0, int_nstage = 0, Sn = 0, xd_off = 0, fx_off = 0, red_off = 0;
+    size_t int_smem = 0;
 };
+
+constexpr int kImmaSplit = 2;  // consumer warps per 16-row tile in qgemv_imma
+
+int imma_nt(size_t m) {
+    const int nt = (int)((3 * m + 7) / 8);
+    return nt <= 3 ? nt : 6;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Shared layout of qgemv_imma: ring, digit planes [3M][Sn], factors
+// [spr][8 NT], block sums [warps][16][8 NT], barriers and flags.
+void plan_imma(TmaPlan &pl, int fmt, size_t m) {
+    if (m > 16) return;
+    const int nt = imma_nt(m);
+    const long long wsb = fmt == 0 ? 128 : 64;
+    const long long sn = (long long)align_up((size_t)(pl.spr * wsb), 128) + 32;
+    const size_t xd = (size_t)(3 * m) * (size_t)sn;
+    const size_t fx = (size_t)pl.spr * 8 * nt * 4;
+    const size_t red = (size_t)kTiles * kImmaSplit * 16 * 8 * nt * 4;
+    for (int ns = kMaxStages; ns >= 2; ns--) {
+        const size_t ring = (size_t)ns * kSlotBytes;
+        const size_t fx_off = align_up(ring + xd, 16);
+        const size_t red_off = align_up(fx_off + fx, 16);
+        const size_t total = red_off + red + 2 * kMaxStages * 8 + 16;
+        if (total <= (size_t)kSmemLimit) {
+            pl.imma = true;
+            pl.int_nt = nt;
+            pl.int_nstage = ns;
+            pl.Sn = (int)sn;
+            pl.xd_off = (int)ring;
+            pl.fx_off = (int)fx_off;
+            pl.red_off = (int)red_off;
+            pl.int_smem = total;
+            return;
+        }
+    }
+}
 
 int padded_stride(int fmt, long long units) {
     long long S = units;
@@ -605,7 +1040,8 @@ TmaPlan make_tma_plan(const QuantSeg *segs, int nseg, size_t m) {
         pl.smem = pl.ring_bytes + xbytes + fixed;
         if (pl.smem <= (size_t)kSmemLimit) break;
     }
-    if (pl.nstage < kMinStages) return pl;
+    plan_imma(pl, w0.format, m);
+    if (pl.nstage < kMinStages && !pl.imma) return pl;
     // Partial slots: the most CTAs that share one block.
     pl.slots = pl.split == 1
                    ? 1
@@ -655,15 +1091,13 @@ bool tensor_maps(const QuantWeight &w, MapPair *out) {
     return true;
 }
 
-template <int FMT, int NT, int SPLIT>
-cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m,
-                       const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws,
-                       uint32_t *err) {
-    TmaArgs a{};
+// Kernel arguments shared by both consumers (tensor maps cached per weight).
+bool fill_args(TmaArgs &a, int fmt, const float *x, const float *x2, size_t m,
+               const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws, uint32_t *err) {
     long long blocks = 0;
     for (int i = 0; i < nseg; i++) {
         MapPair maps;
-        if (!tensor_maps(segs[i].w, &maps)) return cudaErrorInvalidValue;
+        if (!tensor_maps(segs[i].w, &maps)) return false;
         a.codes_map[i] = maps.codes;
         a.scales_map[i] = maps.scales;
         a.out[i] = segs[i].out;
@@ -672,6 +1106,7 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
         a.blk_end[i] = (int)blocks;
     }
     const QuantWeight &w = segs[0].w;
+    const int kstep = fmt == 0 ? Fmt<0>::kStep : Fmt<1>::kStep;
     a.nseg = nseg;
     a.x = x;
     a.x2 = x2;
@@ -679,7 +1114,7 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
     a.K = (int)w.k;
     a.groups = (int)w.groups;
     a.gs_shift = 0;
-    while ((1u << a.gs_shift) < w.group / Fmt<FMT>::kStep) a.gs_shift++;
+    while ((1u << a.gs_shift) < w.group / kstep) a.gs_shift++;
     a.row_bytes = (long long)w.row_bytes;
     a.spr = pl.spr;
     a.total = pl.total;
@@ -693,6 +1128,15 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
     a.err = err;
     a.tickets = static_cast<unsigned *>(ws);
     a.partials = reinterpret_cast<float *>(static_cast<char *>(ws) + 64 * 1024 * sizeof(unsigned));
+    return true;
+}
+
+template <int FMT, int NT, int SPLIT>
+cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m,
+                       const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws,
+                       uint32_t *err) {
+    TmaArgs a{};
+    if (!fill_args(a, FMT, x, x2, m, segs, nseg, pl, ws, err)) return cudaErrorInvalidValue;
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(qgemv_tma<FMT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -702,6 +1146,42 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
     launch_k(qgemv_tma<FMT, NT, SPLIT>, pl.grid, (kTiles * SPLIT + 1) * 32, pl.smem, s, a);
     count_launch();
     return cudaGetLastError();
+}
+
+template <int FMT, int NT>
+cudaError_t launch_imma(cudaStream_t s, const float *x, const float *x2, size_t m,
+                        const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws,
+                        uint32_t *err) {
+    TmaArgs a{};
+    if (!fill_args(a, FMT, x, x2, m, segs, nseg, pl, ws, err)) return cudaErrorInvalidValue;
+    a.nstage = pl.int_nstage;
+    a.Sn = pl.Sn;
+    a.ncol = (int)(3 * m);
+    a.xd_off = pl.xd_off;
+    a.fx_off = pl.fx_off;
+    a.red_off = pl.red_off;
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(qgemv_imma<FMT, NT, kImmaSplit>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        configured = true;
+    }
+    launch_k(qgemv_imma<FMT, NT, kImmaSplit>, pl.grid, (kTiles * kImmaSplit + 1) * 32,
+             pl.int_smem, s, a);
+    count_launch();
+    return cudaGetLastError();
+}
+
+template <int FMT>
+cudaError_t launch_imma_nt(cudaStream_t s, const float *x, const float *x2, size_t m,
+                           const QuantSeg *segs, int nseg, const TmaPlan &pl, void *ws,
+                           uint32_t *err) {
+    switch (pl.int_nt) {
+        case 1: return launch_imma<FMT, 1>(s, x, x2, m, segs, nseg, pl, ws, err);
+        case 2: return launch_imma<FMT, 2>(s, x, x2, m, segs, nseg, pl, ws, err);
+        case 3: return launch_imma<FMT, 3>(s, x, x2, m, segs, nseg, pl, ws, err);
+        default: return launch_imma<FMT, 6>(s, x, x2, m, segs, nseg, pl, ws, err);
+    }
 }
 
 }  // namespace
@@ -733,6 +1213,12 @@ cudaError_t qgemv_tma_group(cudaStream_t s, const float *x, const float *x2, siz
                             const QuantSeg *segs, int nseg, void *workspace, uint32_t *err) {
     TmaPlan pl = make_tma_plan(segs, nseg, m);
     if (!pl.ok || !aligned16(x) || (x2 && !aligned16(x2))) return cudaErrorInvalidValue;
+    // The integer consumer wherever its activation digits fit in shared
+    // memory; the f16 consumer otherwise.
+    if (pl.imma)
+        return segs[0].w.format == 0
+                   ? launch_imma_nt<0>(s, x, x2, m, segs, nseg, pl, workspace, err)
+                   : launch_imma_nt<1>(s, x, x2, m, segs, nseg, pl, workspace, err);
     const int nt = m <= 8 ? 1 : (m <= 16 ? 2 : 4);
     // One column tile: two warps per 16-row tile (17 warps, 96 registers
     // each, no spills); more columns need the registers of one warp per tile.
