@@ -622,98 +622,119 @@ __device__ __forceinline__ float i2f_small(int c) {
     return __int_as_float(c + 0x4B400000) - 12582912.0f;
 }
 
-// Stages all of x as digit planes (consumer warps only): block (m, ws) is
-// handled by one warp, each lane converting 4 (INT4) or 2 (INT8) values.
+// Stages the activation digit planes of warp-steps ws0 .. ws0 + nws - 1
+// (mod spr: the ones this CTA's range touches) for every column (consumer
+// warps only). Block (m, ws) is converted by one warp, each lane taking 4
+// (INT4) or 2 (INT8) values; a warp issues the loads of up to kBatch blocks
+// before converting any, so staging costs about one load latency.
 template <int FMT, int CW, int NT>
-__device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx) {
+__device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, int nws) {
     constexpr int KSTEP = Fmt<FMT>::kStep;
     constexpr int PER = KSTEP / 32;
     constexpr int WSB = Imma<FMT>::kWsBytes;
+    constexpr int kBatch = 4;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int spr = (int)p.spr;
-    const int blocks = p.M * spr;
-    for (int b = warp; b < blocks; b += CW) {
-        const int col = b / spr, st = b - col * spr;
-        const int k0 = st * KSTEP + lane * PER;
-        const float *src = p.x + (long long)col * p.K + k0;
-        float v[PER];
-        if constexpr (PER == 4) {
-            const float4 q = __ldg(reinterpret_cast<const float4 *>(src));
-            v[0] = q.x;
-            v[1] = q.y;
-            v[2] = q.z;
-            v[3] = q.w;
-        } else {
-            const float2 q = __ldg(reinterpret_cast<const float2 *>(src));
-            v[0] = q.x;
-            v[1] = q.y;
-        }
-        if (p.x2) {
-            // SwiGLU: silu(gate) * up, the exact expression of the
-            // elementwise silu_mul kernel.
-            const float *src2 = p.x2 + (long long)col * p.K + k0;
-            float u[PER];
+    const int blocks = p.M * nws;
+    for (int b0 = warp; b0 < blocks; b0 += CW * kBatch) {
+        float v[kBatch][PER], u[kBatch][PER];
+#pragma unroll
+        for (int q = 0; q < kBatch; q++) {
+            const int b = b0 + q * CW;
+            if (b >= blocks) break;
+            const int col = b / nws;
+            int st = ws0 + (b - col * nws);
+            if (st >= spr) st -= spr;
+            const long long off = (long long)col * p.K + st * KSTEP + lane * PER;
             if constexpr (PER == 4) {
-                const float4 q = __ldg(reinterpret_cast<const float4 *>(src2));
-                u[0] = q.x;
-                u[1] = q.y;
-                u[2] = q.z;
-                u[3] = q.w;
+                const float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + off));
+                v[q][0] = a.x;
+                v[q][1] = a.y;
+                v[q][2] = a.z;
+                v[q][3] = a.w;
+                if (p.x2) {
+                    const float4 c = __ldg(reinterpret_cast<const float4 *>(p.x2 + off));
+                    u[q][0] = c.x;
+                    u[q][1] = c.y;
+                    u[q][2] = c.z;
+                    u[q][3] = c.w;
+                }
             } else {
-                const float2 q = __ldg(reinterpret_cast<const float2 *>(src2));
-                u[0] = q.x;
-                u[1] = q.y;
+                const float2 a = __ldg(reinterpret_cast<const float2 *>(p.x + off));
+                v[q][0] = a.x;
+                v[q][1] = a.y;
+                if (p.x2) {
+                    const float2 c = __ldg(reinterpret_cast<const float2 *>(p.x2 + off));
+                    u[q][0] = c.x;
+                    u[q][1] = c.y;
+                }
             }
-#pragma unroll
-            for (int i = 0; i < PER; i++)
-                v[i] = __fmul_rn(__fmul_rn(v[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])))),
-                                 u[i]);
         }
-        float mx = 0.f;
-        bool bad = false;
 #pragma unroll
-        for (int i = 0; i < PER; i++) {
-            const float a = fabsf(v[i]);
-            bad |= !(a <= 3.402823466e38f);  // inf or nan
-            mx = fmaxf(mx, a);
-        }
-        mx = warp_max(mx);
-        bad = __any_sync(0xffffffffu, bad);
-        int e = 0;
-        if (mx > 0.f && !bad) {
-            int ex;
-            frexpf(mx, &ex);
-            e = ex - 6;  // |x| < 2^ex, so |x / 2^e| < 64
-        }
-        int8_t *dst = xd + (3 * col) * p.Sn + st * WSB;
+        for (int q = 0; q < kBatch; q++) {
+            const int b = b0 + q * CW;
+            if (b >= blocks) break;
+            const int col = b / nws;
+            int st = ws0 + (b - col * nws);
+            if (st >= spr) st -= spr;
+            if (p.x2) {
+                // SwiGLU: silu(gate) * up, the exact expression of the
+                // elementwise silu_mul kernel.
 #pragma unroll
-        for (int i = 0; i < PER; i++) {
-            float d0 = 0.f, d1 = 0.f, d2 = 0.f;
-            if (!bad) {
-                const float y = ldexpf(v[i], -e);
-                d0 = rintf(y);
-                float r = (y - d0) * 128.f;
-                d1 = rintf(r);
-                r = (r - d1) * 128.f;
-                d2 = rintf(r);
+                for (int i = 0; i < PER; i++)
+                    v[q][i] = __fmul_rn(
+                        __fmul_rn(v[q][i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[q][i])))),
+                        u[q][i]);
             }
-            const int off = imma_byte<FMT>(lane * PER + i);
-            dst[off] = (int8_t)(int)d0;
-            dst[p.Sn + off] = (int8_t)(int)d1;
-            dst[2 * p.Sn + off] = (int8_t)(int)d2;
-        }
-        if (lane < 3) {
-            // 2^e, times 1/16 for the INT4 codes' byte position; non-finite
-            // input makes the column's outputs NaN.
-            float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
-            f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
-            fx[st * (8 * NT) + 3 * col + lane] = f;
+            float mx = 0.f;
+            bool bad = false;
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                const float a = fabsf(v[q][i]);
+                bad |= !(a <= 3.402823466e38f);  // inf or nan
+                mx = fmaxf(mx, a);
+            }
+            mx = warp_max(mx);
+            bad = __any_sync(0xffffffffu, bad);
+            int e = 0;
+            if (mx > 0.f && !bad) {
+                int ex;
+                frexpf(mx, &ex);
+                e = ex - 6;  // |x| < 2^ex, so |x / 2^e| < 64
+            }
+            int8_t *dst = xd + (3 * col) * p.Sn + st * WSB;
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                float d0 = 0.f, d1 = 0.f, d2 = 0.f;
+                if (!bad) {
+                    const float y = ldexpf(v[q][i], -e);
+                    d0 = rintf(y);
+                    float r = (y - d0) * 128.f;
+                    d1 = rintf(r);
+                    r = (r - d1) * 128.f;
+                    d2 = rintf(r);
+                }
+                const int off = imma_byte<FMT>(lane * PER + i);
+                dst[off] = (int8_t)(int)d0;
+                dst[p.Sn + off] = (int8_t)(int)d1;
+                dst[2 * p.Sn + off] = (int8_t)(int)d2;
+            }
+            if (lane < 3) {
+                // 2^e, times 1/16 for the INT4 codes' byte position;
+                // non-finite input makes the column's outputs NaN.
+                float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
+                f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
+                fx[st * (8 * NT) + 3 * col + lane] = f;
+            }
         }
     }
     // Padding columns 3M .. 8 NT - 1 contribute nothing.
     const int pad = 8 * NT - 3 * p.M;
-    for (int i = threadIdx.x; i < spr * pad; i += CW * 32)
-        fx[(i / pad) * (8 * NT) + 3 * p.M + i % pad] = 0.f;
+    for (int i = threadIdx.x; i < nws * pad; i += CW * 32) {
+        int st = ws0 + i / pad;
+        if (st >= spr) st -= spr;
+        fx[st * (8 * NT) + 3 * p.M + i % pad] = 0.f;
+    }
     consumer_sync<CW>();
 }
 
@@ -827,7 +848,10 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     }
 
     pdl_wait();
-    stage_digits<FMT, CW, NT>(p, xd, fx);
+    // Only the warp-steps this CTA's range touches (contiguous mod spr).
+    const bool all_ws = u1 - u0 >= p.spr;
+    stage_digits<FMT, CW, NT>(p, xd, fx, all_ws ? 0 : (int)(u0 % p.spr),
+                              all_ws ? (int)p.spr : (int)(u1 - u0));
     float res[NT][4];
     int slot = 0, phase = 0;
     for (long long u = u0; u < u1;) {
@@ -909,16 +933,20 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
             dst[m * ld + rbase + tr] = v;
         }
         if (count > 1) {
-            __threadfence();
+            // The barrier orders every thread's partial stores before thread
+            // 0's fence and ticket (release); thread 0's second fence orders
+            // the ticket before the barrier that lets the last CTA read the
+            // other CTAs' partials (acquire).
             consumer_sync<CW>();
             if (threadIdx.x == 0) {
+                __threadfence();
                 const unsigned ticket = atomicAdd(&p.tickets[blk], 1u);
                 *last_flag = ticket == (unsigned)(count - 1);
+                __threadfence();
             }
             consumer_sync<CW>();
             const bool is_last = *last_flag;
             if (is_last) {
-                __threadfence();
                 const int rows_here = min(kBlockRows, n_seg - lblk * kBlockRows);
                 for (int i = threadIdx.x; i < Mc * rows_here; i += CW * 32) {
                     const int c = i / rows_here, r = i % rows_here;
