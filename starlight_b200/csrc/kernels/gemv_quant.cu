@@ -498,8 +498,16 @@ cudaError_t qmatmul(cudaStream_t s, const float *x, size_t m, const QuantWeight 
                     void *workspace, size_t workspace_bytes, uint32_t *err) {
     if (m == 0 || w.n == 0) return cudaSuccess;
     if (w.k == 0) return cudaMemsetAsync(out, 0, m * w.n * sizeof(float), s);
-    // Prefill-sized inputs: one tiled GEMM pass over the weights.
-    if (m > 64) return qgemm_f32(s, x, m, w, out);
+    // Prefill-sized inputs: the tcgen05 GEMM (activation planes after the
+    // GEMV tickets in the workspace), else the SIMT GEMM.
+    if (m > 64) {
+        const size_t tickets = 64 * 1024 * sizeof(unsigned);
+        if (workspace && workspace_bytes > tickets && qgemm_tc_supported(w) &&
+            qgemm_tc_rows_per_pass(w, workspace_bytes - tickets) > 0)
+            return qgemm_tc(s, x, m, w, out, static_cast<char *>(workspace) + tickets,
+                            workspace_bytes - tickets, err);
+        return qgemm_f32(s, x, m, w, out);
+    }
     // Decode-sized inputs: the tensor-core GEMV, in blocks of at most 32 rows.
     for (size_t m0 = 0; m0 < m; m0 += 32) {
         size_t mb = m - m0 < 32 ? m - m0 : 32;

@@ -89,6 +89,13 @@ struct QuantWeight {
     size_t n, k, group, groups, row_bytes;
     int format;            // 0 INT4, 1 INT8
 };
+// Prefill GEMM on the tcgen05 tensor cores (gemm_tc.cu): activations split
+// into bf16 hi/lo planes in `workspace` (rows processed in passes that fit),
+// codes expanded to bf16 in shared memory, group scales applied per group.
+bool qgemm_tc_supported(const QuantWeight &w);
+size_t qgemm_tc_rows_per_pass(const QuantWeight &w, size_t workspace_bytes);
+cudaError_t qgemm_tc(cudaStream_t s, const float *x, size_t m, const QuantWeight &w, float *out,
+                     void *workspace, size_t workspace_bytes, uint32_t *err);
 // Tiled SIMT GEMM with the weight dequantized on load (prefill-sized m).
 cudaError_t qgemm_f32(cudaStream_t s, const float *a, size_t m, const QuantWeight &w, float *out);
 size_t qmatmul_workspace_bytes(const QuantWeight &w, size_t m);

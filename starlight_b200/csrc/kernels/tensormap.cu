@@ -40,5 +40,20 @@ bool encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const voi
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_tensor_map(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                       uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                       uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {row_stride_bytes};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    return fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE,
+              swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace k
 }  // namespace slc

@@ -15,5 +15,11 @@ bool encode_tensor_map_2d(CUtensorMap *map, CUtensorMapDataType dtype, const voi
                           uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
                           uint32_t box_inner, uint32_t box_rows);
 
+// The same with an optional 128-byte swizzle (box_inner * element size must
+// then be at most 128 bytes; the shared destination 1024-byte aligned).
+bool encode_tensor_map(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                       uint64_t inner, uint64_t rows, uint64_t row_stride_bytes,
+                       uint32_t box_inner, uint32_t box_rows, bool swizzle128);
+
 }  // namespace k
 }  // namespace slc

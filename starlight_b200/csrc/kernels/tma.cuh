@@ -122,6 +122,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
         : "memory");
 }
 
+// Tiled 2-D tensor copy global -> shared without a cache hint.
+__device__ __forceinline__ void tma_load_2d_nohint(void *dst, const void *tmap, int x, int y,
+                                                   uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_addr(bar))
+        : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const void *tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }

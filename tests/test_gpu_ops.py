@@ -415,6 +415,23 @@ def test_quantized_matmul_tma_shapes(dev, fmt, m, k, n, group):
     assert err < 1e-4 * max(1.0, (k / 4096) ** 0.5), err
 
 
+@pytest.mark.parametrize("fmt,m,k,n,group", [
+    (orc.INT4, 65, 256, 256, 64),       # one partial M tile, groups of one stage
+    (orc.INT4, 128, 4096, 512, 128),    # 32 groups through both TMEM buffers
+    (orc.INT4, 200, 1024, 700, 128),    # ragged M and N (scalar tail columns)
+    (orc.INT8, 130, 512, 384, 128),
+    (orc.INT4, 96, 192, 260, 192),      # one group of three stages, N % 256 = 4
+    (orc.INT8, 257, 4160, 256, 64),     # K beyond a multiple of 128
+    (orc.INT4, 600, 14336, 256, 128),   # two passes of the activation split
+    (orc.INT8, 512, 4096, 1024, 128),
+])
+def test_quantized_matmul_prefill_tensor_cores(dev, fmt, m, k, n, group):
+    # Prefill-sized M: the tcgen05 GEMM (bf16 hi/lo activations, codes
+    # expanded in shared memory, per-group TMEM partials scaled in f32).
+    err = _qmatmul_case(dev, fmt, m, k, n, group, seed=m * 7 + k + n + group)
+    assert err < 1e-4 * max(1.0, (k / 4096) ** 0.5), err
+
+
 @pytest.mark.parametrize("fmt,k,n", [(orc.INT4, 14336, 4096), (orc.INT4, 4096, 14336),
                                      (orc.INT8, 8192, 1024)])
 def test_quantized_matmul_full_size_spot_rows(dev, fmt, k, n):
