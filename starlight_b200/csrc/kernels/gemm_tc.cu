@@ -25,9 +25,14 @@
 //    group run.
 //
 // Tile 128 (M) x 256 (N) x 64 (K), one CTA per SM (TMEM: 512 columns).
-// Warp 0: TMA producer. Warp 1: TMEM allocation and MMA issue (one thread).
-// Warps 2..9: code conversion, scale promotion and the output epilogue; warp
-// w reads TMEM lanes 32 (w % 4) .. + 31 and columns 128 ((w - 2) / 4) .. + 127.
+// Warp 0: TMA producer of the activation planes. Warp 1: TMEM allocation and
+// MMA issue (one thread). Warp 2: TMA producer of the packed codes, running
+// ahead of the activation ring on its own ring. Warps 3..18: code
+// conversion, scale promotion and the output epilogue; warp w reads TMEM
+// lanes 32 (w % 4) .. + 31 and columns 64 ((w - 3) / 4) .. + 63,
+// accumulating its 32 rows x 64 columns in registers. Group scales reach a
+// warp's lanes by shuffle (no CTA-wide barrier between conversion and
+// promotion).
 //
 // Bound: tensor cores. Algorithmic flops per launch 2 M N K (the hi/lo split
 // executes twice that on the tensor pipe).
@@ -51,12 +56,12 @@ namespace k {
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kConvWarps = 8;
-constexpr int kThreads = (2 + kConvWarps) * 32;  // 320
+constexpr int kConvWarps = 16;
+constexpr int kConv0 = 3;  // first converter warp
+constexpr int kThreads = (kConv0 + kConvWarps) * 32;  // 608
 constexpr int kABytes = BM * BK * 2;             // 16 KiB per plane
 constexpr int kBBytes = BN * BK * 2;             // 32 KiB
 constexpr int kSlotBytes = 2 * kABytes + kBBytes;  // 64 KiB
-constexpr int kPStages = 2;
 constexpr uint32_t kTmemCols = 512;
 // kind::f16, D f32, A bf16, B bf16, both K-major, N = 256, M = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -65,13 +70,13 @@ constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN 
 template <int FMT>
 struct Cfg {
     static constexpr int kStages = FMT == 0 ? 3 : 2;                // bf16 ring
+    static constexpr int kPStages = FMT == 0 ? 3 : 4;               // packed-code ring
     static constexpr int kPackedBytes = FMT == 0 ? BN * BK / 2 : BN * BK;  // per stage
     static constexpr int kRing = kStages * kSlotBytes;
     static constexpr int kPacked = kPStages * kPackedBytes;
-    static constexpr int kScales = 2 * BN * 4;
     static constexpr int kBars = (2 * kStages + 2 * kPStages + 5) * 8 + 16;
     // 1 KiB for aligning the ring to the 1024-byte swizzle atom.
-    static constexpr int kSmem = 1024 + kRing + kPacked + kScales + kBars;
+    static constexpr int kSmem = 1024 + kRing + kPacked + kBars;
 };
 static_assert(Cfg<0>::kSmem <= 227 * 1024, "INT4 shared layout");
 static_assert(Cfg<1>::kSmem <= 227 * 1024, "INT8 shared layout");
@@ -144,10 +149,6 @@ __device__ __forceinline__ void drain_wait(uint64_t *bar, uint32_t parity) {
     }
 }
 
-__device__ __forceinline__ void conv_sync() {
-    asm volatile("bar.sync 1, %0;" ::"r"(kConvWarps * 32) : "memory");
-}
-
 __device__ __forceinline__ uint32_t lop3_and_xor_b(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t d;  // (a & b) ^ c
     asm("lop3.b32 %0, %1, %2, %3, 0x6a;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -209,14 +210,14 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
     unsigned char *smem = smem_raw + ((1024 - (raw & 1023)) & 1023);
     unsigned char *ring = smem;
     unsigned char *packed = smem + C::kRing;
-    float *sc = reinterpret_cast<float *>(packed + C::kPacked);  // [2][BN]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(sc + 2 * BN);
-    uint64_t *full = bars;                // [S]: A bytes + 8 converter warps
+    uint64_t *bars = reinterpret_cast<uint64_t *>(packed + C::kPacked);
+    constexpr int kPStages = C::kPStages;
+    uint64_t *full = bars;                // [S]: A bytes + converter warps
     uint64_t *empty = full + S;           // [S]: MMA commit
-    uint64_t *pfull = empty + S;          // [2]: packed bytes
-    uint64_t *pempty = pfull + kPStages;  // [2]: 8 converter warps
+    uint64_t *pfull = empty + S;          // [P]: packed bytes
+    uint64_t *pempty = pfull + kPStages;  // [P]: converter warps
     uint64_t *afull = pempty + kPStages;  // [2]: MMA commit of a group
-    uint64_t *aempty = afull + 2;         // [2]: 8 converter warps
+    uint64_t *aempty = afull + 2;         // [2]: converter warps
     uint64_t *done = aempty + 2;          // [1]: final MMA commit
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -257,12 +258,10 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ---- TMA producer.
+        // ---- TMA producer of the activation planes.
         if (lane == 0) {
             prefetch_tensormap(&p.a_hi);
             prefetch_tensormap(&p.a_lo);
-            prefetch_tensormap(&p.codes);
-            const uint64_t pol_w = policy_evict_first();
             pdl_wait();  // activations come from the split kernel
             int issued = 0;
             for (int s = 0; s < nst; s++) {
@@ -272,21 +271,28 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
                 mbar_arrive_expect_tx(&full[slot], 2 * kABytes);
                 tma_load_2d_nohint(sl, &p.a_hi, s * BK, m0, &full[slot]);
                 tma_load_2d_nohint(sl + kABytes, &p.a_lo, s * BK, m0, &full[slot]);
-                const int ps = s % kPStages, pph = (s / kPStages) & 1;
-                if (s >= kPStages && !mbar_wait(&pempty[ps], pph ^ 1, p.err, abort)) {
-                    // The A copies of this stage are in flight: count them.
-                    issued = s + 1;
-                    break;
-                }
-                mbar_arrive_expect_tx(&pfull[ps], C::kPackedBytes);
-                tma_load_2d(packed + ps * C::kPackedBytes, &p.codes,
-                            FMT == 0 ? s * (BK / 2) : s * BK, n0, &pfull[ps], pol_w);
                 issued = s + 1;
             }
             // Copies still in flight must land before the CTA's shared memory
             // is released: wait (bounded) for the last stages' barriers.
             for (int s = issued - 1; s >= 0 && s >= issued - S; s--)
                 drain_wait(&full[s % S], (s / S) & 1);
+        }
+    } else if (warp == 2) {
+        // ---- TMA producer of the packed codes (weights: no dependency on
+        // the previous kernel).
+        if (lane == 0) {
+            prefetch_tensormap(&p.codes);
+            const uint64_t pol_w = policy_evict_first();
+            int issued = 0;
+            for (int s = 0; s < nst; s++) {
+                const int ps = s % kPStages, pph = (s / kPStages) & 1;
+                if (s >= kPStages && !mbar_wait(&pempty[ps], pph ^ 1, p.err, abort)) break;
+                mbar_arrive_expect_tx(&pfull[ps], C::kPackedBytes);
+                tma_load_2d(packed + ps * C::kPackedBytes, &p.codes,
+                            FMT == 0 ? s * (BK / 2) : s * BK, n0, &pfull[ps], pol_w);
+                issued = s + 1;
+            }
             for (int s = issued - 1; s >= 0 && s >= issued - kPStages; s--)
                 drain_wait(&pfull[s % kPStages], (s / kPStages) & 1);
         }
@@ -320,45 +326,54 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
             drain_wait(done, 0);
         }
     } else {
-        // ---- converters / promotion / epilogue (warps 2..9).
+        // ---- converters / promotion / epilogue (warps 3..18).
         pdl_wait();
-        const int cw = warp - 2;
-        const int tc = cw * 32 + lane;  // 0..255
+        const int cw = warp - kConv0;
+        const int tc = cw * 32 + lane;  // 0 .. 511
         const int q = warp & 3;         // TMEM lane quarter
-        const int hh = cw >> 2;         // column half
-        float acc[128];
+        const int cq = cw >> 2;         // column quarter
+        const int cbase = n0 + cq * 64; // this warp's first output column
+        float acc[64];
 #pragma unroll
-        for (int i = 0; i < 128; i++) acc[i] = 0.f;
+        for (int i = 0; i < 64; i++) acc[i] = 0.f;
+        // Scales of this warp's columns cbase + lane and cbase + 32 + lane:
+        // group `cur` (being accumulated) and the next one (prefetched).
+        float cur0 = 0.f, cur1 = 0.f;
 
-        auto promote = [&](int g) {
-            conv_sync();  // scales of g visible; ordered after earlier readers
+        auto promote = [&](int g, float s0, float s1) {
             const int buf = g & 1;
             bool ok = !*abort && mbar_wait(&afull[buf], (g >> 1) & 1, p.err, abort);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
             if (ok) {
                 tc_fence_after();
-                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + hh * 128);
-                const float *sg = sc + buf * BN + hh * 128;
+                const uint32_t ta =
+                    tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN + cq * 64);
 #pragma unroll
-                for (int c = 0; c < 8; c++) {
+                for (int c = 0; c < 4; c++) {
                     float v[16];
                     tmem_ld16(ta + c * 16, v);
 #pragma unroll
-                    for (int j = 0; j < 16; j++) acc[c * 16 + j] = fmaf(v[j], sg[c * 16 + j], acc[c * 16 + j]);
+                    for (int j = 0; j < 16; j++) {
+                        const int col = c * 16 + j;  // 0..63: lane col % 32 of s0 / s1
+                        const float sj = __shfl_sync(0xffffffffu, col < 32 ? s0 : s1, col & 31);
+                        acc[col] = fmaf(v[j], sj, acc[col]);
+                    }
                 }
                 tc_fence_before();
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&aempty[buf]);
-            conv_sync();  // the next group's scales may overwrite this buffer
         };
 
         for (int s = 0; s < nst; s++) {
             const int kbase = s * BK;
             const int g = kbase / G;
-            if (kbase % G == 0) {
-                const int n = n0 + tc;
-                sc[(g & 1) * BN + tc] = n < p.N ? __ldg(p.scales + (size_t)n * p.groups + g) : 0.f;
+            const bool first = kbase % G == 0;
+            float nxt0 = 0.f, nxt1 = 0.f;
+            if (first) {
+                const int c0 = cbase + lane, c1 = cbase + 32 + lane;
+                nxt0 = c0 < p.N ? __ldg(p.scales + (size_t)c0 * p.groups + g) : 0.f;
+                nxt1 = c1 < p.N ? __ldg(p.scales + (size_t)c1 * p.groups + g) : 0.f;
             }
             const int slot = s % S, ph = (s / S) & 1;
             const int ps = s % kPStages, pph = (s / kPStages) & 1;
@@ -367,9 +382,9 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
             if (ok) {
                 const unsigned char *pk = packed + ps * C::kPackedBytes;
                 const uint32_t bb = smem_addr(ring + slot * kSlotBytes + 2 * kABytes);
-#pragma unroll 2
-                for (int j = 0; j < 8; j++) {
-                    const int item = tc + 256 * j;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int item = tc + 512 * j;
                     const int r = item >> 3, c = item & 7;
                     uint4 v;
                     if (FMT == 0)
@@ -385,25 +400,28 @@ __global__ void __launch_bounds__(kThreads, 1) qgemm_tc_kernel(const __grid_cons
                 mbar_arrive(&full[slot]);
                 mbar_arrive(&pempty[ps]);
             }
-            // Promote the previous group while the MMAs of this one run.
-            if (kbase % G == 0 && g >= 1) promote(g - 1);
+            if (first) {
+                // Promote the previous group while the MMAs of this one run.
+                if (g >= 1) promote(g - 1, cur0, cur1);
+                cur0 = nxt0;
+                cur1 = nxt1;
+            }
         }
-        promote((nst * BK - 1) / G);
+        promote((nst * BK - 1) / G, cur0, cur1);
 
-        // ---- epilogue: row m0 + 32 q + lane, columns n0 + 128 hh ...
+        // ---- epilogue: row m0 + 32 q + lane, columns cbase .. cbase + 63.
         const int row = m0 + q * 32 + lane;
         if (row < p.M && !*abort) {
             float *orow = p.out + (size_t)row * p.N;
-            const int c0 = n0 + hh * 128;
-            if ((p.N & 3) == 0 && c0 + 128 <= p.N) {
+            if ((p.N & 3) == 0 && cbase + 64 <= p.N) {
 #pragma unroll
-                for (int i = 0; i < 32; i++)
-                    *reinterpret_cast<float4 *>(orow + c0 + 4 * i) =
+                for (int i = 0; i < 16; i++)
+                    *reinterpret_cast<float4 *>(orow + cbase + 4 * i) =
                         make_float4(acc[4 * i], acc[4 * i + 1], acc[4 * i + 2], acc[4 * i + 3]);
             } else {
 #pragma unroll
-                for (int i = 0; i < 128; i++)
-                    if (c0 + i < p.N) orow[c0 + i] = acc[i];
+                for (int i = 0; i < 64; i++)
+                    if (cbase + i < p.N) orow[cbase + i] = acc[i];
             }
         }
     }
