@@ -66,14 +66,14 @@ constexpr int kTiles = 8;                         // 16-row tiles per block
 constexpr int kTileRows = 16;                     // rows per tile (mma M)
 constexpr int kBlockRows = kTileRows * kTiles;    // 128 rows per block
 constexpr int kStepBytes = 64;                    // bytes per row per warp-step
-constexpr int kRun = 3;                           // warp-steps per stage
-constexpr int kPitch = kRun * kStepBytes;         // 192 bytes: = 64 mod 128, so the 16-byte
+constexpr int kRun = 5;                           // warp-steps per stage
+constexpr int kPitch = kRun * kStepBytes;         // 320 bytes: = 64 mod 128, so the 16-byte
                                                   // reads of rows g and g + 1 never collide
 constexpr int kScaleBox = 8;                      // scale groups per row per stage (box)
-constexpr int kCodeBytes = kBlockRows * kPitch;   // 24 KiB
+constexpr int kCodeBytes = kBlockRows * kPitch;   // 40 KiB
 constexpr int kScaleBytes = kBlockRows * kScaleBox * 4;
-constexpr int kSlotBytes = kCodeBytes + kScaleBytes;  // 28 KiB
-constexpr int kMaxStages = 8;
+constexpr int kSlotBytes = kCodeBytes + kScaleBytes;  // 44 KiB
+constexpr int kMaxStages = 5;
 constexpr int kMinStages = 3;
 constexpr int kSmemLimit = 227 * 1024;
 
@@ -702,7 +702,7 @@ __device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, i
                 frexpf(mx, &ex);
                 e = ex - 6;  // |x| < 2^ex, so |x / 2^e| < 64
             }
-            int8_t *dst = xd + (3 * col) * p.Sn + (b - col * nws) * WSB;
+            int8_t *dst = xd + (3 * col) * p.Sn + st * WSB;
 #pragma unroll
             for (int i = 0; i < PER; i++) {
                 float d0 = 0.f, d1 = 0.f, d2 = 0.f;
@@ -724,14 +724,17 @@ __device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, i
                 // non-finite input makes the column's outputs NaN.
                 float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
                 f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
-                fx[(b - col * nws) * (8 * NT) + 3 * col + lane] = f;
+                fx[st * (8 * NT) + 3 * col + lane] = f;
             }
         }
     }
     // Padding columns 3M .. 8 NT - 1 contribute nothing.
     const int pad = 8 * NT - 3 * p.M;
-    for (int i = threadIdx.x; i < nws * pad; i += CW * 32)
-        fx[(i / pad) * (8 * NT) + 3 * p.M + i % pad] = 0.f;
+    for (int i = threadIdx.x; i < nws * pad; i += CW * 32) {
+        int st = ws0 + i / pad;
+        if (st >= spr) st -= spr;
+        fx[st * (8 * NT) + 3 * p.M + i % pad] = 0.f;
+    }
     consumer_sync<CW>();
 }
 
@@ -778,8 +781,8 @@ __device__ __forceinline__ void imma_step(const unsigned char *rowg, int pitch,
 template <int FMT, int NT, int SPLIT, bool FULL>
 __device__ __forceinline__ void imma_stage(const TmaArgs &p, const unsigned char *base,
                                            const float *ssl, int step0, int run, int h,
-                                           const unsigned char *xd, const float *fx, int ws0,
-                                           int g, int t, float (&res)[NT][4]) {
+                                           const unsigned char *xd, const float *fx, int g, int t,
+                                           float (&res)[NT][4]) {
     constexpr int WSB = Imma<FMT>::kWsBytes;
     const int g4 = (step0 >> p.gs_shift) & ~3;
 #pragma unroll
@@ -788,15 +791,13 @@ __device__ __forceinline__ void imma_stage(const TmaArgs &p, const unsigned char
         if (j < kRun && (FULL || j < run)) {
             int c[NT][4];
             const int sw = step0 + j;
-            int lsw = sw - ws0;  // position among the staged warp-steps
-            if (lsw < 0) lsw += (int)p.spr;
-            imma_step<FMT, NT>(base + j * kStepBytes, kPitch, xd + lsw * WSB + t * 8, p.Sn,
+            imma_step<FMT, NT>(base + j * kStepBytes, kPitch, xd + sw * WSB + t * 8, p.Sn,
                                p.ncol, g, c);
             const int gi = (sw >> p.gs_shift) - g4;
             const float s0 = ssl[gi], s1 = ssl[8 * kScaleBox + gi];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const float2 f = *reinterpret_cast<const float2 *>(fx + lsw * (8 * NT) + 8 * nt + 2 * t);
+                const float2 f = *reinterpret_cast<const float2 *>(fx + sw * (8 * NT) + 8 * nt + 2 * t);
                 res[nt][0] = fmaf(i2f_small(c[nt][0]), s0 * f.x, res[nt][0]);
                 res[nt][1] = fmaf(i2f_small(c[nt][1]), s0 * f.y, res[nt][1]);
                 res[nt][2] = fmaf(i2f_small(c[nt][2]), s1 * f.x, res[nt][2]);
@@ -849,8 +850,8 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     pdl_wait();
     // Only the warp-steps this CTA's range touches (contiguous mod spr).
     const bool all_ws = u1 - u0 >= p.spr;
-    const int ws0 = all_ws ? 0 : (int)(u0 % p.spr);
-    stage_digits<FMT, CW, NT>(p, xd, fx, ws0, all_ws ? (int)p.spr : (int)(u1 - u0));
+    stage_digits<FMT, CW, NT>(p, xd, fx, all_ws ? 0 : (int)(u0 % p.spr),
+                              all_ws ? (int)p.spr : (int)(u1 - u0));
     float res[NT][4];
     int slot = 0, phase = 0;
     for (long long u = u0; u < u1;) {
@@ -877,11 +878,11 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
                 if (run == kRun)
                     imma_stage<FMT, NT, SPLIT, true>(p, base, ssl, step0, run, h,
                                                      reinterpret_cast<const unsigned char *>(xd),
-                                                     fx, ws0, g, t, res);
+                                                     fx, g, t, res);
                 else
                     imma_stage<FMT, NT, SPLIT, false>(p, base, ssl, step0, run, h,
                                                       reinterpret_cast<const unsigned char *>(xd),
-                                                      fx, ws0, g, t, res);
+                                                      fx, g, t, res);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -984,46 +985,43 @@ int imma_nt(size_t m) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Shared layout of qgemv_imma: ring, digit planes [3M][Sn] and factors
-// [nws][8 NT] for the nws warp-steps a CTA can touch, block sums
-// [warps][16][8 NT], barriers and flags. The largest ring that keeps the
-// footprint within half an SM's shared memory (so that the next launch's
-// CTAs are resident, and stream their weights, while this one finishes),
-// else the largest that fits at all.
-constexpr size_t kHalfSm = 113 * 1024;
-
+// Shared layout of qgemv_imma: ring, digit planes [3M][Sn], factors
+// [spr][8 NT], block sums [warps][16][8 NT], barriers and flags.
 void plan_imma(TmaPlan &pl, int fmt, size_t m) {
     if (m > 16) return;
     const int nt = imma_nt(m);
     const long long wsb = fmt == 0 ? 128 : 64;
-    const long long nws =
-        pl.split == 1 ? pl.spr : std::min<long long>(pl.spr, (pl.units + pl.grid - 1) / pl.grid);
-    const long long sn = (long long)align_up((size_t)(nws * wsb), 128) + 32;
+    const long long sn = (long long)align_up((size_t)(pl.spr * wsb), 128) + 32;
     const size_t xd = (size_t)(3 * m) * (size_t)sn;
-    const size_t fx = (size_t)nws * 8 * nt * 4;
+    const size_t fx = (size_t)pl.spr * 8 * nt * 4;
     const size_t red = (size_t)kTiles * kImmaSplit * 16 * 8 * nt * 4;
-    auto total = [&](int ns, size_t *fx_off, size_t *red_off) {
+    for (int ns = kMaxStages; ns >= 2; ns--) {
         const size_t ring = (size_t)ns * kSlotBytes;
-        *fx_off = align_up(ring + xd, 16);
-        *red_off = align_up(*fx_off + fx, 16);
-        return *red_off + red + 2 * kMaxStages * 8 + 16;
-    };
-    for (const size_t limit : {kHalfSm, (size_t)kSmemLimit}) {
-        for (int ns = kMaxStages; ns >= 3; ns--) {
-            size_t fx_off, red_off;
-            const size_t t = total(ns, &fx_off, &red_off);
-            if (t > limit) continue;
+        const size_t fx_off = align_up(ring + xd, 16);
+        const size_t red_off = align_up(fx_off + fx, 16);
+        const size_t total = red_off + red + 2 * kMaxStages * 8 + 16;
+        if (total <= (size_t)kSmemLimit) {
             pl.imma = true;
             pl.int_nt = nt;
             pl.int_nstage = ns;
             pl.Sn = (int)sn;
-            pl.xd_off = ns * kSlotBytes;
+            pl.xd_off = (int)ring;
             pl.fx_off = (int)fx_off;
             pl.red_off = (int)red_off;
-            pl.int_smem = t;
+            pl.int_smem = total;
             return;
         }
     }
+}
+
+int padded_stride(int fmt, long long units) {
+    long long S = units;
+    if (fmt == 0) {
+        while (S % 8 != 4) S++;
+    } else if (S % 2 == 0) {
+        S++;
+    }
+    return (int)S;
 }
 
 // One matrix the kernel can stream: shape, format and alignment rules.
