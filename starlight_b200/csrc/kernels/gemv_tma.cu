@@ -1239,6 +1239,9 @@ bool qgemv_tma_x_aligned(const float *x) { return aligned16(x); }
 
 cudaError_t qgemv_tma_group(cudaStream_t s, const float *x, const float *x2, size_t m,
                             const QuantSeg *segs, int nseg, void *workspace, uint32_t *err) {
+    // One or two activation rows: whole tiles per CTA (no split-K tail).
+    if (m <= 2 && aligned16(x) && (!x2 || aligned16(x2)) && qgemv_lane_supported(segs, nseg, m))
+        return qgemv_lane_group(s, x, x2, m, segs, nseg, err);
     TmaPlan pl = make_tma_plan(segs, nseg, m);
     if (!pl.ok || !aligned16(x) || (x2 && !aligned16(x2))) return cudaErrorInvalidValue;
     // The integer consumer wherever its activation digits fit in shared

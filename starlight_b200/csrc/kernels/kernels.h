@@ -111,6 +111,11 @@ struct QuantSeg {
     QuantWeight w;
     float *out;  // [m, w.n]
 };
+// Decode GEMV for M <= 2 (gemv_lane.cu): whole 16-row tiles per CTA, no
+// workspace; used by qgemv_tma_group where its plan fits.
+bool qgemv_lane_supported(const QuantSeg *segs, int nseg, size_t m);
+cudaError_t qgemv_lane_group(cudaStream_t s, const float *x, const float *x2, size_t m,
+                             const QuantSeg *segs, int nseg, uint32_t *err);
 bool qgemv_tma_group_supported(const QuantSeg *segs, int nseg, size_t m);
 size_t qgemv_tma_group_workspace_bytes(const QuantSeg *segs, int nseg, size_t m);
 cudaError_t qgemv_tma_group(cudaStream_t s, const float *x, const float *x2, size_t m,
