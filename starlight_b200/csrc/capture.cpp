@@ -216,10 +216,29 @@ static int matmul_run(const std::vector<Rec> &v, size_t i) {
 }
 
 // Runs the pending commands; dyn = kernels read the device scalar table
-// (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs.
+// (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs;
+// the decode attention block (SplitHeads x3, Rope x2, CausalAttention,
+// MergeHeads at seq 1) goes out as the fused two-launch block.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     const std::vector<Rec> &v = cs->pending;
     for (size_t i = 0; i < v.size();) {
+        if (v[i].op.code == SLC_OP_SPLIT_HEADS && i + 7 <= v.size() &&
+            v[i + 5].op.code == SLC_OP_CAUSAL_ATTENTION) {
+            BlockMember bm[7];
+            for (int t = 0; t < 7; t++) {
+                const Rec &r = v[i + t];
+                bm[t] = BlockMember{&r.op, r.in, r.iv, r.n_in, r.out, r.ov, r.scalars, r.n_scalars};
+            }
+            const Rec &at = v[i + 5];
+            const uint32_t *ds = (dyn && at.slot >= 0) ? cs->d_table + at.slot : nullptr;
+            bool launched = false;
+            int rc = slc_launch_attention_block(d, bm, ds, &launched);
+            if (rc != SLC_OK) return rc;
+            if (launched) {
+                i += 7;
+                continue;
+            }
+        }
         const int run = matmul_run(v, i);
         if (run > 1) {
             MatmulMember mm[4];

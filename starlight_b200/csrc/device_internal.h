@@ -91,6 +91,22 @@ struct MatmulMember {
     const slc_value *ov;
 };
 int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched);
+// The seven-command decode attention block (SplitHeads q, k, v; Rope q, k;
+// CausalAttention; MergeHeads), each command already validated: launched as
+// the fused decode block when its conditions hold (*launched = true);
+// otherwise nothing is launched.
+struct BlockMember {
+    const slc_op *op;
+    const slc_buffer_ref *in;
+    const slc_value *iv;
+    uint64_t n_in;
+    const slc_buffer_ref *out;
+    const slc_value *ov;
+    const uint32_t *scalars;
+    uint64_t n_scalars;
+};
+int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
+                               bool *launched);
 // Try to record a validated command for graph replay. Returns 1 if the
 // command was recorded (launch deferred), 0 if it must be launched now.
 int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

@@ -285,6 +285,7 @@ struct DecodeParams {
     const float *v_new;
     float *cache;
     float *out;            // [B, H, 1, D]
+    float *out2;           // optional second copy of out (merged heads, same layout at seq 1)
     float *part_o;         // [B * H][chunks][D]
     float *part_ml;        // [B * H][chunks][2]
     unsigned *tickets;     // [B * Hkv]
@@ -463,7 +464,9 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         }
         const long long row = (long long)b * p.H + kvh * G + r;
         if (p.chunks == 1) {
-            p.out[row * D + d] = __fdiv_rn(acc, ll);
+            const float val = __fdiv_rn(acc, ll);
+            p.out[row * D + d] = val;
+            if (p.out2) p.out2[row * D + d] = val;
         } else {
             p.part_o[(row * p.chunks + chunk) * D + d] = acc;
             if (d == 0) {
@@ -547,7 +550,9 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         const int idx = threadIdx.x + j * kDecThreads;
         if (idx < G * D) {
             const int r = idx / D, d = idx - r * D;
-            p.out[(row0 + r) * D + d] = __fdiv_rn(acc[j], sm_inv[r]);
+            const float val = __fdiv_rn(acc[j], sm_inv[r]);
+            p.out[(row0 + r) * D + d] = val;
+            if (p.out2) p.out2[(row0 + r) * D + d] = val;
         }
     }
     if (threadIdx.x == 0) p.tickets[bh] = 0u;  // ready for the next launch
@@ -589,6 +594,95 @@ DecodePlan plan_decode(size_t batch, size_t kv_heads, size_t heads, size_t seq, 
     return pl;
 }
 
+// ---- fused decode attention block (capture-time fusion) ------------------
+//
+// Replaces, for one decode position (seq 1), the command run
+//   SplitHeads(q) -> qs, SplitHeads(k) -> ks, SplitHeads(v) -> vs,
+//   Rope(qs) -> qr, Rope(ks) -> kr, CausalAttention(qr, kr, vs) -> a,
+//   MergeHeads(a) -> am
+// by two launches with the same results in every output buffer:
+//  * decode_block_prep (one CTA) reads q, k, v and the positions into shared
+//    memory, then writes qs, ks, vs, qr, kr in command order, a block-wide
+//    barrier between commands, so outputs that share bytes with each other
+//    or with the inputs (the memory plan reuses dead temporaries) end with
+//    the values sequential execution leaves. It also writes qr, kr and v to
+//    a private scratch area that nothing else aliases.
+//  * attention_decode reads only the scratch copies and writes a and am.
+// At seq 1, [B, 1, H * D] and [B, H, 1, D] are the same bytes, so the split
+// and merge copies are element copies. RoPE is the rope_kernel arithmetic
+// (f64 angle from the host-computed f64 denominators, f32 rotation).
+struct BlockPrep {
+    const float *q, *k, *v;
+    const uint32_t *pos;  // [B, 1]
+    float *qs, *ks, *vs, *qr, *kr;
+    float *sq, *sk, *sv;  // private scratch copies: roped q, roped k, v
+    int B, H, Hkv, D, gptj;
+    double denom[64];     // theta^(2 p / D), host libm pow
+};
+
+__device__ __forceinline__ void rope_pair(const float *x, float *o, int base, int p, int half,
+                                          int gptj, const float *trig) {
+    const int i0 = gptj ? base + 2 * p : base + p;
+    const int i1 = gptj ? base + 2 * p + 1 : base + p + half;
+    const float first = x[i0], second = x[i1];
+    const float sn = trig[p], cs = trig[half + p];
+    o[i0] = __fsub_rn(__fmul_rn(first, cs), __fmul_rn(second, sn));
+    o[i1] = __fadd_rn(__fmul_rn(first, sn), __fmul_rn(second, cs));
+}
+
+__global__ void __launch_bounds__(1024) decode_block_prep(const __grid_constant__ BlockPrep p) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float sm[];
+    const int D = p.D, half = D / 2;
+    const int nq = p.B * p.H * D, nk = p.B * p.Hkv * D;
+    float *q = sm, *k = q + nq, *v = k + nk, *trig = v + nk;  // trig [B][D]
+    float *rq = trig + p.B * D, *rk = rq + nq;                  // roped q, k
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) q[i] = p.q[i];
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+        k[i] = p.k[i];
+        v[i] = p.v[i];
+    }
+    for (int i = threadIdx.x; i < p.B * half; i += blockDim.x) {
+        const int b = i / half, pr = i - b * half;
+        const double angle = (double)p.pos[b] / p.denom[pr];
+        double sn, cs;
+        sincos(angle, &sn, &cs);
+        trig[b * D + pr] = (float)sn;
+        trig[b * D + half + pr] = (float)cs;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < p.B * p.H * half; i += blockDim.x) {
+        const int row = i / half, pr = i - row * half;  // row = b * H + h
+        rope_pair(q, rq, row * D, pr, half, p.gptj, trig + (row / p.H) * D);
+    }
+    for (int i = threadIdx.x; i < p.B * p.Hkv * half; i += blockDim.x) {
+        const int row = i / half, pr = i - row * half;
+        rope_pair(k, rk, row * D, pr, half, p.gptj, trig + (row / p.Hkv) * D);
+    }
+    __syncthreads();  // rotated rows are read by other threads below
+    // Private copies for the attention kernel.
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) p.sq[i] = rq[i];
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+        p.sk[i] = rk[i];
+        p.sv[i] = v[i];
+    }
+    // The five outputs, in command order.
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) p.qs[i] = q[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) p.ks[i] = k[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) p.vs[i] = v[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) p.qr[i] = rq[i];
+    __syncthreads();
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) p.kr[i] = rk[i];
+}
+
+size_t block_prep_smem(size_t B, size_t H, size_t Hkv, size_t D) {
+    return (2 * B * H * D + 3 * B * Hkv * D + B * D) * sizeof(float);
+}
+
 }  // namespace
 
 cudaError_t kv_append(cudaStream_t s, const float *k, const float *v, float *cache,
@@ -614,6 +708,68 @@ size_t attention_workspace_bytes(size_t batch, size_t heads, size_t kv_heads, si
     return batch * heads * seq * pl.chunks * (head_dim + 2) * sizeof(float);
 }
 
+// Decode attention (seq 1) with the append fused: q / k / v rows given,
+// out (and, if set, out2) written. Requires the decode plan.
+cudaError_t causal_attention_decode_into(cudaStream_t s, const float *q, const float *k,
+                                         const float *v, float *cache, float *out, float *out2,
+                                         const KvGeometry &g, size_t heads, size_t past_len,
+                                         float scale, const AttnScratch &scr,
+                                         const uint32_t *d_past) {
+    const size_t keys = d_past ? g.max_seq : past_len + 1;
+    const size_t time_stride = g.kv_heads * g.head_dim;
+    const size_t parity_stride = g.max_seq * time_stride;
+    DecodePlan dp = plan_decode(g.batch, g.kv_heads, heads, 1, g.head_dim, keys);
+    if (!dp.ok || g.batch * g.kv_heads > scr.ticket_count) return cudaErrorInvalidValue;
+    const size_t need = dp.chunks <= 1 ? 0 : g.batch * heads * dp.chunks * (g.head_dim + 2) * 4;
+    if (need > scr.workspace_bytes) return cudaErrorMemoryAllocation;
+    DecodeParams p{};
+    p.q = q;
+    p.k_new = k;
+    p.v_new = v;
+    p.cache = cache;
+    p.out = out;
+    p.out2 = out2;
+    p.part_o = static_cast<float *>(scr.workspace);
+    p.part_ml = p.part_o + g.batch * heads * dp.chunks * g.head_dim;
+    p.tickets = scr.tickets;
+    p.d_past = d_past;
+    p.err = scr.err;
+    p.batch_stride = (long long)(g.layers * 2 * parity_stride);
+    p.layer_off = (long long)(g.layer * 2 * parity_stride);
+    p.parity_stride = (long long)parity_stride;
+    p.time_stride = (long long)time_stride;
+    p.past = (int)past_len;
+    p.max_seq = (int)g.max_seq;
+    p.H = (int)heads;
+    p.Hkv = (int)g.kv_heads;
+    p.G = (int)(heads / g.kv_heads);
+    p.chunk_keys = dp.chunk_keys;
+    p.chunks = dp.chunks;
+    p.scale = scale;
+    dim3 grid((unsigned)dp.chunks, (unsigned)(g.batch * g.kv_heads));
+    const bool d128 = g.head_dim == 128;
+    switch (p.G) {
+    case 1:
+        launch_k(d128 ? attention_decode<4, 1, 8> : attention_decode<2, 1, 8>, grid,
+                 kDecThreads, 0, s, p);
+        break;
+    case 2:
+        launch_k(d128 ? attention_decode<4, 2, 8> : attention_decode<2, 2, 8>, grid,
+                 kDecThreads, 0, s, p);
+        break;
+    case 4:
+        launch_k(d128 ? attention_decode<4, 4, 8> : attention_decode<2, 4, 8>, grid,
+                 kDecThreads, 0, s, p);
+        break;
+    default:
+        launch_k(d128 ? attention_decode<4, 8, 4> : attention_decode<2, 8, 4>, grid,
+                 kDecThreads, 0, s, p);
+        break;
+    }
+    count_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, const float *v,
                              float *cache, float *out, const KvGeometry &g, size_t heads,
                              size_t seq, size_t past_len, float scale, const AttnScratch &scr,
@@ -623,55 +779,9 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
     const size_t time_stride = g.kv_heads * g.head_dim;
     const size_t parity_stride = g.max_seq * time_stride;
     DecodePlan dp = plan_decode(g.batch, g.kv_heads, heads, seq, g.head_dim, keys);
-    if (dp.ok && g.batch * g.kv_heads <= scr.ticket_count) {
-        const size_t need = dp.chunks <= 1 ? 0 : g.batch * heads * dp.chunks * (g.head_dim + 2) * 4;
-        if (need > scr.workspace_bytes) return cudaErrorMemoryAllocation;
-        DecodeParams p{};
-        p.q = q;
-        p.k_new = k;
-        p.v_new = v;
-        p.cache = cache;
-        p.out = out;
-        p.part_o = static_cast<float *>(scr.workspace);
-        p.part_ml = p.part_o + g.batch * heads * dp.chunks * g.head_dim;
-        p.tickets = scr.tickets;
-        p.d_past = d_past;
-        p.err = scr.err;
-        p.batch_stride = (long long)(g.layers * 2 * parity_stride);
-        p.layer_off = (long long)(g.layer * 2 * parity_stride);
-        p.parity_stride = (long long)parity_stride;
-        p.time_stride = (long long)time_stride;
-        p.past = (int)past_len;
-        p.max_seq = (int)g.max_seq;
-        p.H = (int)heads;
-        p.Hkv = (int)g.kv_heads;
-        p.G = (int)(heads / g.kv_heads);
-        p.chunk_keys = dp.chunk_keys;
-        p.chunks = dp.chunks;
-        p.scale = scale;
-        dim3 grid((unsigned)dp.chunks, (unsigned)(g.batch * g.kv_heads));
-        const bool d128 = g.head_dim == 128;
-        switch (p.G) {
-        case 1:
-            launch_k(d128 ? attention_decode<4, 1, 8> : attention_decode<2, 1, 8>, grid,
-                     kDecThreads, 0, s, p);
-            break;
-        case 2:
-            launch_k(d128 ? attention_decode<4, 2, 8> : attention_decode<2, 2, 8>, grid,
-                     kDecThreads, 0, s, p);
-            break;
-        case 4:
-            launch_k(d128 ? attention_decode<4, 4, 8> : attention_decode<2, 4, 8>, grid,
-                     kDecThreads, 0, s, p);
-            break;
-        default:
-            launch_k(d128 ? attention_decode<4, 8, 4> : attention_decode<2, 8, 4>, grid,
-                     kDecThreads, 0, s, p);
-            break;
-        }
-        count_launch();
-        return cudaGetLastError();
-    }
+    if (dp.ok && g.batch * g.kv_heads <= scr.ticket_count)
+        return causal_attention_decode_into(s, q, k, v, cache, out, nullptr, g, heads, past_len,
+                                            scale, scr, d_past);
     cudaError_t e = kv_append(s, k, v, cache, g, past_len, seq, d_past);
     if (e != cudaSuccess) return e;
     Plan pl = plan(g.batch, heads, g.kv_heads, seq, keys - seq, g.head_dim);
@@ -716,6 +826,57 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
         count_launch();
     }
     return cudaGetLastError();
+}
+
+size_t decode_block_scratch_floats(size_t batch, size_t heads, size_t kv_heads, size_t head_dim) {
+    return batch * (heads + 2 * kv_heads) * head_dim;
+}
+
+bool decode_block_supported(size_t batch, size_t heads, size_t kv_heads, size_t head_dim,
+                            size_t keys_max, size_t ticket_count) {
+    DecodePlan dp = plan_decode(batch, kv_heads, heads, 1, head_dim, keys_max);
+    return dp.ok && head_dim / 2 <= 64 && batch * kv_heads <= ticket_count &&
+           block_prep_smem(batch, heads, kv_heads, head_dim) <= 200 * 1024;
+}
+
+cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, float *cache,
+                                   const KvGeometry &g, size_t heads, size_t past_len, float scale,
+                                   float theta, int gptj, const AttnScratch &scr,
+                                   const uint32_t *d_past) {
+    BlockPrep bp{};
+    bp.q = io.q;
+    bp.k = io.k;
+    bp.v = io.v;
+    bp.pos = io.pos;
+    bp.qs = io.qs;
+    bp.ks = io.ks;
+    bp.vs = io.vs;
+    bp.qr = io.qr;
+    bp.kr = io.kr;
+    const size_t nq = g.batch * heads * g.head_dim, nk = g.batch * g.kv_heads * g.head_dim;
+    bp.sq = io.scratch;
+    bp.sk = bp.sq + nq;
+    bp.sv = bp.sk + nk;
+    bp.B = (int)g.batch;
+    bp.H = (int)heads;
+    bp.Hkv = (int)g.kv_heads;
+    bp.D = (int)g.head_dim;
+    bp.gptj = gptj;
+    for (size_t pr = 0; pr < g.head_dim / 2; pr++)
+        bp.denom[pr] = pow((double)theta, 2.0 * (double)pr / (double)g.head_dim);
+    const size_t smem = block_prep_smem(g.batch, heads, g.kv_heads, g.head_dim);
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(decode_block_prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             200 * 1024);
+        configured = true;
+    }
+    launch_k(decode_block_prep, 1, 1024, smem, s, bp);
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return causal_attention_decode_into(s, bp.sq, bp.sk, bp.sv, cache, io.out, io.out_merged, g,
+                                        heads, past_len, scale, scr, d_past);
 }
 
 }  // namespace k

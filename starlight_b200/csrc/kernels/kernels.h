@@ -75,6 +75,24 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
                              size_t seq, size_t past_len, float scale, const AttnScratch &scr,
                              const uint32_t *d_past = nullptr);
 
+// Decode (seq 1) attention block: SplitHeads q/k/v, Rope q/k, causal
+// attention with the KV append, MergeHeads, as two launches that leave every
+// output buffer as the seven commands would (attention.cu).
+struct DecodeBlockIo {
+    const float *q, *k, *v;  // [B, 1, H * D], [B, 1, Hkv * D] x 2
+    const uint32_t *pos;     // [B, 1]
+    float *qs, *ks, *vs, *qr, *kr;
+    float *out, *out_merged;
+    float *scratch;          // decode_block_scratch_floats(...) floats, private
+};
+size_t decode_block_scratch_floats(size_t batch, size_t heads, size_t kv_heads, size_t head_dim);
+bool decode_block_supported(size_t batch, size_t heads, size_t kv_heads, size_t head_dim,
+                            size_t keys_max, size_t ticket_count);
+cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, float *cache,
+                                   const KvGeometry &g, size_t heads, size_t past_len, float scale,
+                                   float theta, int gptj, const AttnScratch &scr,
+                                   const uint32_t *d_past);
+
 // ---- matmul_f32.cu --------------------------------------------------------------
 // out[b] = a[b or 0] . w[b or 0]^T (NT) or a . w (NN), batch broadcast when a
 // batch count is 1 (device.rs:1301-1407).

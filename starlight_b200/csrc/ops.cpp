@@ -682,6 +682,84 @@ int slc_launch_command(slc_device *d, const slc_op *op, const slc_buffer_ref *in
     return run_op(d, c, true);
 }
 
+namespace {
+bool same_ref(const slc_buffer_ref &a, const slc_buffer_ref &b) {
+    return a.buffer == b.buffer && a.offset == b.offset && a.len == b.len;
+}
+bool disjoint(const slc_buffer_ref &a, const slc_buffer_ref &b) {
+    return a.buffer != b.buffer || a.offset + a.len <= b.offset || b.offset + b.len <= a.offset;
+}
+}  // namespace
+
+int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
+                               bool *launched) {
+    *launched = false;
+    const BlockMember &sq = bm[0], &sk = bm[1], &sv = bm[2], &rq = bm[3], &rk = bm[4],
+                      &at = bm[5], &mh = bm[6];
+    const uint16_t want[7] = {SLC_OP_SPLIT_HEADS, SLC_OP_SPLIT_HEADS, SLC_OP_SPLIT_HEADS,
+                              SLC_OP_ROPE,        SLC_OP_ROPE,        SLC_OP_CAUSAL_ATTENTION,
+                              SLC_OP_MERGE_HEADS};
+    for (int i = 0; i < 7; i++)
+        if (bm[i].op->code != want[i]) return SLC_OK;
+    // Dataflow: split outputs feed the ropes / attention, rope outputs feed
+    // the attention, the attention output feeds the merge.
+    if (sq.n_in != 1 || sk.n_in != 1 || sv.n_in != 1 || rq.n_in != 2 || rk.n_in != 2 ||
+        at.n_in != 4 || mh.n_in != 1 || at.n_scalars != 1)
+        return SLC_OK;
+    if (!same_ref(rq.in[0], sq.out[0]) || !same_ref(rk.in[0], sk.out[0]) ||
+        !same_ref(at.in[0], rq.out[0]) || !same_ref(at.in[1], rk.out[0]) ||
+        !same_ref(at.in[2], sv.out[0]) || !same_ref(mh.in[0], at.out[0]) ||
+        !same_ref(rq.in[1], rk.in[1]) || at.iv[3].role != SLC_ROLE_STATE)
+        return SLC_OK;
+    if (rq.op->rope_variant != rk.op->rope_variant || rq.op->theta != rk.op->theta ||
+        rq.op->rope_variant > SLC_ROPE_GPTJ)
+        return SLC_OK;
+    const slc_value &qv = at.iv[0];  // [B, H, 1, D]
+    if (qv.rank != 4 || qv.dims[2] != 1) return SLC_OK;
+    const uint64_t B = qv.dims[0], H = qv.dims[1], D = qv.dims[3];
+    const uint64_t Hkv = at.op->kv_heads;
+    const slc_value &st = at.iv[3];  // [B, layers, 2, max_seq, Hkv, D]
+    if (st.rank != 6) return SLC_OK;
+    const uint64_t layers = st.dims[1], max_seq = st.dims[3];
+    const uint64_t past = at.scalars[0];
+    const uint64_t keys = dyn_past ? max_seq : past + 1;
+    if (!k::decode_block_supported(B, H, Hkv, D, keys, kAttnTicketBytes / sizeof(unsigned)))
+        return SLC_OK;
+    const uint64_t need_scratch = k::decode_block_scratch_floats(B, H, Hkv, D);
+    const uint64_t need_part =
+        k::attention_workspace_bytes(B, H, Hkv, 1, past, D, max_seq, dyn_past != nullptr);
+    if (need_scratch > intermediate_floats(d) || need_part > kernel_scratch_bytes(d))
+        return SLC_OK;
+    // The merged output is written together with the attention output: it
+    // must not share bytes with it (the merge reads it).
+    if (!disjoint(mh.out[0], at.out[0])) return SLC_OK;
+    auto fp = [&](const slc_buffer_ref &r) {
+        return reinterpret_cast<float *>(d->buffers[r.buffer].ptr) + r.offset;
+    };
+    k::DecodeBlockIo io{};
+    io.q = fp(sq.in[0]);
+    io.k = fp(sk.in[0]);
+    io.v = fp(sv.in[0]);
+    io.pos = reinterpret_cast<const uint32_t *>(d->buffers[rq.in[1].buffer].ptr) + rq.in[1].offset;
+    io.qs = fp(sq.out[0]);
+    io.ks = fp(sk.out[0]);
+    io.vs = fp(sv.out[0]);
+    io.qr = fp(rq.out[0]);
+    io.kr = fp(rk.out[0]);
+    io.out = fp(at.out[0]);
+    io.out_merged = fp(mh.out[0]);
+    io.scratch = intermediates(d);
+    k::KvGeometry g{B, layers, at.op->layer, Hkv, D, max_seq};
+    k::AttnScratch scr{kernel_scratch(d), kernel_scratch_bytes(d), ws_attn_tickets(d),
+                       kAttnTicketBytes / sizeof(unsigned), d->device_flag};
+    cudaError_t e = k::decode_attention_block(d->stream, io, fp(at.in[3]), g, H, past,
+                                              at.op->scale, rq.op->theta,
+                                              rq.op->rope_variant == SLC_ROPE_GPTJ, scr, dyn_past);
+    if (e != cudaSuccess) return slc_fail(d, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
+    *launched = true;
+    return SLC_OK;
+}
+
 int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched) {
     *launched = false;
     if (n < 2 || n > 4) return SLC_OK;

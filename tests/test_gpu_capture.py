@@ -184,3 +184,80 @@ def test_grouped_matmuls_under_capture():
     st = dev.capture_stats()
     assert st["captures"] == 1 and st["replays"] == 2
     dev.close()
+
+
+
+@pytest.mark.parametrize("heads,kv_heads,head_dim,batch", [(4, 4, 64, 1), (8, 2, 128, 1),
+                                                           (4, 1, 128, 2)])
+def test_fused_decode_attention_block_matches_commands(heads, kv_heads, head_dim, batch):
+    # With capture on, the decode command run SplitHeads x3 -> Rope x2 ->
+    # CausalAttention -> MergeHeads goes out as the fused two-launch block.
+    # Every byte of the buffers it writes and the KV cache must equal the
+    # command-by-command results, also where outputs reuse the bytes of dead
+    # values as the engine's memory plan does: ks over q, vs over k, kr over
+    # qs, am over qr (each command's own inputs and outputs stay disjoint).
+    from starlight_b200.device import BufferRef
+    B, H, Hkv, D, L, S, past = batch, heads, kv_heads, head_dim, 2, 40, 17
+    lcg = Lcg(heads * 7 + head_dim)
+    nq, nk = B * H * D, B * Hkv * D
+    q0 = lcg.normal(nq, 0.0, 1.0)
+    k0 = lcg.normal(nk, 0.0, 1.0)
+    v0 = lcg.normal(nk, 0.0, 1.0)
+    cache0 = lcg.normal(B * L * 2 * S * Hkv * D, 0.0, 1.0)
+    pos = np.full(B, past, np.uint32)
+    Q0 = nq + 2 * nk          # qs
+    Q1 = Q0 + nq              # qr
+    A = Q1 + nq               # a
+    total = A + nq
+    arena0 = np.zeros(total, np.float32)
+    arena0[0:nq] = q0
+    arena0[nq:nq + nk] = k0
+    arena0[nq + nk:nq + 2 * nk] = v0
+
+    def run(capture):
+        dev = CudaDevice(0)
+        if capture:
+            dev.set_capture(True)
+        ar = dev.allocate_f32(total)
+        cache = dev.allocate_f32(cache0.size)
+        pb = dev.allocate_u32(B)
+        dev.upload_u32(pb, pos)
+        R = lambda o, n: BufferRef(ar, o, n)
+        q, k, v = R(0, nq), R(nq, nk), R(nq + nk, nk)
+        qs, qr, a = R(Q0, nq), R(Q1, nq), R(A, nq)
+        ks, vs, kr, am = R(0, nk), R(nq, nk), R(Q0, nk), R(Q1, nq)
+        pref, cref = BufferRef(pb, 0, B), BufferRef(cache, 0, cache0.size)
+        st = Value(DType.F32, (B, L, 2, S, Hkv, D), ValueRole.State)
+        sq = Op(OpCode.SplitHeads, heads=H, head_dim=D)
+        skv = Op(OpCode.SplitHeads, heads=Hkv, head_dim=D)
+        rope = Op(OpCode.Rope, theta=10000.0)
+        att = Op(OpCode.CausalAttention, layer=1, heads=H, kv_heads=Hkv, head_dim=D,
+                 scale=1.0 / math.sqrt(D))
+        mh = Op(OpCode.MergeHeads, heads=H, head_dim=D)
+        results = []
+        for _ in range(3 if capture else 1):  # eager run, capture, replay
+            dev.upload_f32(ar, arena0)
+            dev.upload_f32(cache, cache0)
+            dev.dispatch(sq, [q], [F((B, 1, H * D))], [qs], [F((B, H, 1, D))])
+            dev.dispatch(skv, [k], [F((B, 1, Hkv * D))], [ks], [F((B, Hkv, 1, D))])
+            dev.dispatch(skv, [v], [F((B, 1, Hkv * D))], [vs], [F((B, Hkv, 1, D))])
+            dev.dispatch(rope, [qs, pref], [F((B, H, 1, D)), Value.u32((B, 1))], [qr],
+                         [F((B, H, 1, D))])
+            dev.dispatch(rope, [ks, pref], [F((B, Hkv, 1, D)), Value.u32((B, 1))], [kr],
+                         [F((B, Hkv, 1, D))])
+            dev.dispatch(att, [qr, kr, vs, cref],
+                         [F((B, H, 1, D)), F((B, Hkv, 1, D)), F((B, Hkv, 1, D)), st], [a],
+                         [F((B, H, 1, D))], scalars=[past])
+            dev.dispatch(mh, [a], [F((B, H, 1, D))], [am], [F((B, 1, H * D))])
+            dev.synchronize()
+            results.append((get(dev, R(0, total)), get(dev, cref)))
+        stats = dev.capture_stats() if capture else None
+        dev.close()
+        return results, stats
+
+    (eager,), _ = run(False)
+    fused, stats = run(True)
+    assert stats["replays"] >= 1
+    for arena, cache in fused:
+        np.testing.assert_array_equal(arena, eager[0])
+        np.testing.assert_array_equal(cache, eager[1])
