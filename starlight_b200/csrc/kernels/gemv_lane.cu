@@ -229,79 +229,113 @@ __global__ void __launch_bounds__(kThreads, 1) qgemv_lane(const __grid_constant_
     for (int i = 0; i < kDepth - 1; i++) issue(i);
 
     pdl_wait();
-    // ---- this warp's activation digits and factors.
+    // ---- this warp's activation digits and factors. The loads of up to
+    // kStageBatch warp-steps are issued before any conversion, so staging
+    // costs about one load latency per batch.
     int8_t *dig = reinterpret_cast<int8_t *>(smem + p.dig_off) + warp * (p.wmax * 3 * p.M * WSB);
     float *fxw = reinterpret_cast<float *>(smem + p.fx_off) + warp * (p.wmax * 8);
     const int ncol = 3 * p.M;
-    for (int q = 0; q < nw; q++) {
-        const int ws = ws0 + q;
-#pragma unroll 1
-        for (int m = 0; m < p.M; m++) {
-            const long long off = (long long)m * p.K + ws * KSTEP + lane * PER;
-            float v[PER], u[PER];
-            if constexpr (PER == 4) {
-                const float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + off));
-                v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+    constexpr int kStageBatch = 8;
+    for (int m = 0; m < p.M; m++) {
+        for (int q0 = 0; q0 < nw; q0 += kStageBatch) {
+            float v[kStageBatch][PER], u[kStageBatch][PER];
+#pragma unroll
+            for (int qq = 0; qq < kStageBatch; qq++) {
+                const int q = q0 + qq;
+                if (q >= nw) break;
+                const long long off = (long long)m * p.K + (ws0 + q) * KSTEP + lane * PER;
+                if constexpr (PER == 4) {
+                    const float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + off));
+                    v[qq][0] = a.x, v[qq][1] = a.y, v[qq][2] = a.z, v[qq][3] = a.w;
+                    if (p.x2) {
+                        const float4 b = __ldg(reinterpret_cast<const float4 *>(p.x2 + off));
+                        u[qq][0] = b.x, u[qq][1] = b.y, u[qq][2] = b.z, u[qq][3] = b.w;
+                    }
+                } else {
+                    const float2 a = __ldg(reinterpret_cast<const float2 *>(p.x + off));
+                    v[qq][0] = a.x, v[qq][1] = a.y;
+                    if (p.x2) {
+                        const float2 b = __ldg(reinterpret_cast<const float2 *>(p.x2 + off));
+                        u[qq][0] = b.x, u[qq][1] = b.y;
+                    }
+                }
+            }
+#pragma unroll
+            for (int qq = 0; qq < kStageBatch; qq++) {
+                const int q = q0 + qq;
+                if (q >= nw) break;
                 if (p.x2) {
-                    const float4 b = __ldg(reinterpret_cast<const float4 *>(p.x2 + off));
-                    u[0] = b.x, u[1] = b.y, u[2] = b.z, u[3] = b.w;
-                }
-            } else {
-                const float2 a = __ldg(reinterpret_cast<const float2 *>(p.x + off));
-                v[0] = a.x, v[1] = a.y;
-                if (p.x2) {
-                    const float2 b = __ldg(reinterpret_cast<const float2 *>(p.x2 + off));
-                    u[0] = b.x, u[1] = b.y;
-                }
-            }
-            if (p.x2) {
-                // SwiGLU: silu(gate) * up, the elementwise silu_mul expression.
+                    // SwiGLU: silu(gate) * up, the elementwise silu_mul expression.
 #pragma unroll
-                for (int i = 0; i < PER; i++)
-                    v[i] = __fmul_rn(__fmul_rn(v[i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[i])))),
-                                     u[i]);
-            }
-            float mx = 0.f;
-            bool bad = false;
-#pragma unroll
-            for (int i = 0; i < PER; i++) {
-                const float a = fabsf(v[i]);
-                bad |= !(a <= 3.402823466e38f);
-                mx = fmaxf(mx, a);
-            }
-            mx = warp_max(mx);
-            bad = __any_sync(0xffffffffu, bad);
-            int e = 0;
-            if (mx > 0.f && !bad) {
-                int ex;
-                frexpf(mx, &ex);
-                e = ex - 6;  // |x / 2^e| < 64
-            }
-            int8_t *d0p = dig + ((q * ncol) + 3 * m) * WSB;
-#pragma unroll
-            for (int i = 0; i < PER; i++) {
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f;
-                if (!bad) {
-                    const float y = ldexpf(v[i], -e);
-                    d0 = rintf(y);
-                    float r = (y - d0) * 128.f;
-                    d1 = rintf(r);
-                    r = (r - d1) * 128.f;
-                    d2 = rintf(r);
+                    for (int i = 0; i < PER; i++)
+                        v[qq][i] = __fmul_rn(
+                            __fmul_rn(v[qq][i], __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-v[qq][i])))),
+                            u[qq][i]);
                 }
-                const int b = lane_byte<FMT>(lane * PER + i);
-                d0p[b] = (int8_t)(int)d0;
-                d0p[WSB + b] = (int8_t)(int)d1;
-                d0p[2 * WSB + b] = (int8_t)(int)d2;
-            }
-            if (lane < 3) {
-                float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
-                f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
-                fxw[q * 8 + 3 * m + lane] = f;
+                float mx = 0.f;
+                bool bad = false;
+#pragma unroll
+                for (int i = 0; i < PER; i++) {
+                    const float a = fabsf(v[qq][i]);
+                    bad |= !(a <= 3.402823466e38f);
+                    mx = fmaxf(mx, a);
+                }
+                mx = warp_max(mx);
+                bad = __any_sync(0xffffffffu, bad);
+                int e = 0;
+                if (mx > 0.f && !bad) {
+                    int ex;
+                    frexpf(mx, &ex);
+                    e = ex - 6;  // |x / 2^e| < 64
+                }
+                // Digits: y = x / 2^e exactly (power-of-two multiply; ldexpf
+                // outside the normal exponent range), then
+                // d = rint(y), y' = (y - d) * 128 = fma(d, -128, 128 y), exact.
+                float sc;
+                const bool direct = e >= -126 && e <= 126;
+                sc = __int_as_float((127 - e) << 23);
+                uint32_t db[3][PER];  // digit + 1.5 * 2^23, low byte = two's complement
+#pragma unroll
+                for (int i = 0; i < PER; i++) {
+                    float y = 0.f;
+                    if (!bad) y = direct ? v[qq][i] * sc : ldexpf(v[qq][i], -e);
+                    const float d0 = rintf(y);
+                    const float r1 = fmaf(d0, -128.f, y * 128.f);
+                    const float d1 = rintf(r1);
+                    const float r2 = fmaf(d1, -128.f, r1 * 128.f);
+                    const float d2 = rintf(r2);
+                    db[0][i] = __float_as_uint(d0 + 12582912.0f);
+                    db[1][i] = __float_as_uint(d1 + 12582912.0f);
+                    db[2][i] = __float_as_uint(d2 + 12582912.0f);
+                }
+                unsigned char *d0p =
+                    reinterpret_cast<unsigned char *>(dig + ((q * ncol) + 3 * m) * WSB);
+#pragma unroll
+                for (int dd = 0; dd < 3; dd++) {
+                    if (FMT == 0) {
+                        // Values i = 0, 2 -> bytes B, B + 1; i = 1, 3 -> B + 4, B + 5.
+                        const int b = lane_byte<FMT>(lane * PER);
+                        *reinterpret_cast<uint16_t *>(d0p + dd * WSB + b) =
+                            (uint16_t)prmt(db[dd][0], db[dd][2], 0x0040u);
+                        *reinterpret_cast<uint16_t *>(d0p + dd * WSB + b + 4) =
+                            (uint16_t)prmt(db[dd][1], db[dd][3 % PER], 0x0040u);
+                    } else {
+                        // Values i = 0, 1 -> adjacent bytes.
+                        const int b = lane_byte<FMT>(lane * PER);
+                        *reinterpret_cast<uint16_t *>(d0p + dd * WSB + b) =
+                            (uint16_t)prmt(db[dd][0], db[dd][1 % PER], 0x0040u);
+                    }
+                }
+                if (lane < 3) {
+                    float f = bad ? __int_as_float(0x7fc00000) : ldexpf(FMT == 0 ? 0.0625f : 1.0f, e);
+                    f *= lane == 0 ? 1.0f : (lane == 1 ? 0.0078125f : 6.103515625e-05f);
+                    fxw[q * 8 + 3 * m + lane] = f;
+                }
             }
         }
-        if (lane >= ncol && lane < 8) fxw[q * 8 + lane] = 0.f;
     }
+    for (int q = 0; q < nw; q++)
+        if (lane >= ncol && lane < 8) fxw[q * 8 + lane] = 0.f;
     __syncwarp();
 
     float *red = reinterpret_cast<float *>(smem + p.red_off);  // [kBatch][kWarps][32]
