@@ -218,7 +218,8 @@ static int matmul_run(const std::vector<Rec> &v, size_t i) {
 // Runs the pending commands; dyn = kernels read the device scalar table
 // (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs;
 // the decode attention block (SplitHeads x3, Rope x2, CausalAttention,
-// MergeHeads at seq 1) goes out as the fused two-launch block.
+// MergeHeads at seq 1) goes out as the fused two-launch block, and a residual
+// Add followed by the RmsNorm of its sum as one launch.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     const std::vector<Rec> &v = cs->pending;
     for (size_t i = 0; i < v.size();) {
@@ -236,6 +237,21 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
             if (rc != SLC_OK) return rc;
             if (launched) {
                 i += 7;
+                continue;
+            }
+        }
+        if (v[i].op.code == SLC_OP_ADD && i + 1 < v.size() &&
+            v[i + 1].op.code == SLC_OP_RMS_NORM) {
+            const Rec &ra = v[i], &rr = v[i + 1];
+            const BlockMember add{&ra.op, ra.in, ra.iv, ra.n_in, ra.out, ra.ov, ra.scalars,
+                                  ra.n_scalars};
+            const BlockMember rms{&rr.op, rr.in, rr.iv, rr.n_in, rr.out, rr.ov, rr.scalars,
+                                  rr.n_scalars};
+            bool launched = false;
+            int rc = slc_launch_add_rmsnorm(d, &add, &rms, &launched);
+            if (rc != SLC_OK) return rc;
+            if (launched) {
+                i += 2;
                 continue;
             }
         }

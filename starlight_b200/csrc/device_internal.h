@@ -107,6 +107,10 @@ struct BlockMember {
 };
 int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
                                bool *launched);
+// Add(a, b) -> sum followed by RmsNorm(sum, w) -> out, both validated:
+// launched as one kernel when the shapes and buffer reuse allow it.
+int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMember *rms,
+                           bool *launched);
 // Try to record a validated command for graph replay. Returns 1 if the
 // command was recorded (launch deferred), 0 if it must be launched now.
 int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

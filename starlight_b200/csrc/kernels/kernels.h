@@ -25,6 +25,12 @@ cudaError_t copy_f32(cudaStream_t s, const float *src, float *dst, size_t n);
 // ---- reductions (norm.cu, softmax.cu) --------------------------------------
 cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out, size_t rows,
                      size_t hidden, float eps);
+// Residual Add then RmsNorm in one launch: sum = a + b, out = rms_norm(sum).
+// Supported where rms_norm itself keeps a row in registers.
+bool add_rms_norm_supported(const float *a, const float *b, const float *sum, const float *w,
+                            const float *out, size_t rows, size_t hidden);
+cudaError_t add_rms_norm(cudaStream_t s, const float *a, const float *b, float *sum,
+                         const float *w, float *out, size_t rows, size_t hidden, float eps);
 cudaError_t softmax(cudaStream_t s, const float *x, float *out, size_t rows, size_t cols);
 cudaError_t softmax_causal(cudaStream_t s, const float *x, float *out, size_t rows, size_t cols,
                            size_t seq, size_t past_len);

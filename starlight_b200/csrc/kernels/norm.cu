@@ -21,8 +21,14 @@ __device__ __forceinline__ float inv_rms(float sum_sq, size_t hidden, float eps)
 }
 
 // One CTA of 256 threads per row, NV float4 per thread kept in registers.
-template <int NV>
+// RESID: the row is first formed as x + x2 (the residual Add, one IEEE add
+// per element, the elementwise kernel's expression), written to sum_out, and
+// then normalised: the Add -> RmsNorm pair in one launch. Every read of a row
+// precedes the CTA barrier and every write follows it.
+template <int NV, bool RESID>
 __global__ void __launch_bounds__(256) rms_norm_regs(const float *__restrict__ x,
+                                                     const float *__restrict__ x2,
+                                                     float *__restrict__ sum_out,
                                                      const float *__restrict__ w,
                                                      float *__restrict__ out, size_t rows,
                                                      size_t hidden, float eps) {
@@ -39,6 +45,11 @@ __global__ void __launch_bounds__(256) rms_norm_regs(const float *__restrict__ x
             size_t c = threadIdx.x + (size_t)i * 256;
             if (c < h4) {
                 v[i] = ld_stream_f4(xr + 4 * c);
+                if (RESID) {
+                    const float4 b = ld_stream_f4(x2 + row * hidden + 4 * c);
+                    v[i] = make_float4(__fadd_rn(v[i].x, b.x), __fadd_rn(v[i].y, b.y),
+                                       __fadd_rn(v[i].z, b.z), __fadd_rn(v[i].w, b.w));
+                }
                 ss += v[i].x * v[i].x + v[i].y * v[i].y + v[i].z * v[i].z + v[i].w * v[i].w;
             }
         }
@@ -54,6 +65,7 @@ __global__ void __launch_bounds__(256) rms_norm_regs(const float *__restrict__ x
         for (int i = 0; i < NV; i++) {
             size_t c = threadIdx.x + (size_t)i * 256;
             if (c < h4) {
+                if (RESID) *reinterpret_cast<float4 *>(sum_out + row * hidden + 4 * c) = v[i];
                 float4 g = *reinterpret_cast<const float4 *>(w + 4 * c);
                 float4 r = make_float4(__fmul_rn(__fmul_rn(v[i].x, inv), g.x),
                                        __fmul_rn(__fmul_rn(v[i].y, inv), g.y),
@@ -152,16 +164,45 @@ cudaError_t rms_norm(cudaStream_t s, const float *x, const float *w, float *out,
     if (hidden <= 1024 && rows >= 64) {
         launch_k(rms_norm_warp, grid_for(rows, 8, 16), 256, 0, s, x, w, out, rows, hidden, eps);
     } else if (vec && h4 <= 256) {
-        launch_k(rms_norm_regs<1>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<1, false>, grid, 256, 0, s, x, nullptr, nullptr, w, out, rows, hidden,
+                 eps);
     } else if (vec && h4 <= 512) {
-        launch_k(rms_norm_regs<2>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<2, false>, grid, 256, 0, s, x, nullptr, nullptr, w, out, rows, hidden,
+                 eps);
     } else if (vec && h4 <= 1024) {
-        launch_k(rms_norm_regs<4>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<4, false>, grid, 256, 0, s, x, nullptr, nullptr, w, out, rows, hidden,
+                 eps);
     } else if (vec && h4 <= 2048) {
-        launch_k(rms_norm_regs<8>, grid, 256, 0, s, x, w, out, rows, hidden, eps);
+        launch_k(rms_norm_regs<8, false>, grid, 256, 0, s, x, nullptr, nullptr, w, out, rows, hidden,
+                 eps);
     } else {
         launch_k(rms_norm_generic, grid, 256, 0, s, x, w, out, rows, hidden, eps);
     }
+    count_launch();
+    return cudaGetLastError();
+}
+
+bool add_rms_norm_supported(const float *a, const float *b, const float *sum, const float *w,
+                            const float *out, size_t rows, size_t hidden) {
+    const bool vec = hidden % 4 == 0 && aligned16(a) && aligned16(b) && aligned16(sum) &&
+                     aligned16(w) && aligned16(out);
+    // Exactly the cases rms_norm serves with rms_norm_regs.
+    return rows > 0 && vec && hidden / 4 <= 2048 && !(hidden <= 1024 && rows >= 64);
+}
+
+cudaError_t add_rms_norm(cudaStream_t s, const float *a, const float *b, float *sum,
+                         const float *w, float *out, size_t rows, size_t hidden, float eps) {
+    if (!add_rms_norm_supported(a, b, sum, w, out, rows, hidden)) return cudaErrorInvalidValue;
+    const size_t h4 = hidden / 4;
+    const int grid = (int)(rows < (size_t)kSmCount * 16 ? rows : (size_t)kSmCount * 16);
+    if (h4 <= 256)
+        launch_k(rms_norm_regs<1, true>, grid, 256, 0, s, a, b, sum, w, out, rows, hidden, eps);
+    else if (h4 <= 512)
+        launch_k(rms_norm_regs<2, true>, grid, 256, 0, s, a, b, sum, w, out, rows, hidden, eps);
+    else if (h4 <= 1024)
+        launch_k(rms_norm_regs<4, true>, grid, 256, 0, s, a, b, sum, w, out, rows, hidden, eps);
+    else
+        launch_k(rms_norm_regs<8, true>, grid, 256, 0, s, a, b, sum, w, out, rows, hidden, eps);
     count_launch();
     return cudaGetLastError();
 }

@@ -760,6 +760,34 @@ int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint3
     return SLC_OK;
 }
 
+int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMember *rms,
+                           bool *launched) {
+    *launched = false;
+    if (add->op->code != SLC_OP_ADD || rms->op->code != SLC_OP_RMS_NORM || add->n_in != 2 ||
+        rms->n_in != 2 || !same_ref(rms->in[0], add->out[0]))
+        return SLC_OK;
+    const slc_value &xv = rms->iv[0];
+    if (xv.rank < 1 || xv.dtype != SLC_F32) return SLC_OK;
+    const uint64_t hidden = xv.dims[xv.rank - 1];
+    uint64_t rows = 1;
+    for (uint32_t r = 0; r + 1 < xv.rank; r++) rows *= xv.dims[r];
+    // Rows are read before the barrier and written after it by the same
+    // CTA; across rows an output may only reuse the inputs' bytes when there
+    // is a single row.
+    if (rows != 1 && (!disjoint(rms->out[0], add->in[0]) || !disjoint(rms->out[0], add->in[1])))
+        return SLC_OK;
+    auto fp = [&](const slc_buffer_ref &r) {
+        return reinterpret_cast<float *>(d->buffers[r.buffer].ptr) + r.offset;
+    };
+    const float *a = fp(add->in[0]), *b = fp(add->in[1]), *w = fp(rms->in[1]);
+    float *sum = fp(add->out[0]), *out = fp(rms->out[0]);
+    if (!k::add_rms_norm_supported(a, b, sum, w, out, rows, hidden)) return SLC_OK;
+    if (k::add_rms_norm(d->stream, a, b, sum, w, out, rows, hidden, rms->op->eps) != cudaSuccess)
+        return slc_fail(d, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
+    *launched = true;
+    return SLC_OK;
+}
+
 int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched) {
     *launched = false;
     if (n < 2 || n > 4) return SLC_OK;

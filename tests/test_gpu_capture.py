@@ -261,3 +261,45 @@ def test_fused_decode_attention_block_matches_commands(heads, kv_heads, head_dim
     for arena, cache in fused:
         np.testing.assert_array_equal(arena, eager[0])
         np.testing.assert_array_equal(cache, eager[1])
+
+
+@pytest.mark.parametrize("rows,hidden,reuse", [(1, 4096, True), (1, 256, True), (3, 4096, False),
+                                               (5, 1024, True)])
+def test_fused_add_rms_norm_matches_commands(rows, hidden, reuse):
+    # Add(a, b) -> s then RmsNorm(s) -> o goes out as one launch with capture
+    # on. With reuse the norm's output takes the bytes of the dead addend a
+    # (fused only for a single row; otherwise the two commands run as such):
+    # every byte must equal command-by-command execution.
+    from starlight_b200.device import BufferRef
+    lcg = Lcg(rows * 13 + hidden)
+    n = rows * hidden
+    a0, b0 = lcg.normal(n, 0.0, 1.0), lcg.normal(n, 0.0, 1.0)
+    w0 = lcg.normal(hidden, 1.0, 0.1)
+    total = 4 * n
+
+    def run(capture):
+        dev = CudaDevice(0)
+        if capture:
+            dev.set_capture(True)
+        ar = dev.allocate_f32(total)
+        wb = dev.allocate_f32(hidden)
+        dev.upload_f32(wb, w0)
+        a, b, s = BufferRef(ar, 0, n), BufferRef(ar, n, n), BufferRef(ar, 2 * n, n)
+        o = BufferRef(ar, 0, n) if reuse else BufferRef(ar, 3 * n, n)
+        init = np.zeros(total, np.float32)
+        init[:n], init[n:2 * n] = a0, b0
+        shape = (rows, hidden)
+        outs = []
+        for _ in range(3 if capture else 1):
+            dev.upload_f32(ar, init)
+            dev.dispatch(Op(OpCode.Add), [a, b], [F(shape), F(shape)], [s], [F(shape)])
+            dev.dispatch(Op(OpCode.RmsNorm, eps=1e-5), [s, BufferRef(wb, 0, hidden)],
+                         [F(shape), F((hidden,))], [o], [F(shape)])
+            dev.synchronize()
+            outs.append(get(dev, BufferRef(ar, 0, total)))
+        dev.close()
+        return outs
+
+    (eager,) = run(False)
+    for got in run(True):
+        np.testing.assert_array_equal(got, eager)
