@@ -215,6 +215,25 @@ static int matmul_run(const std::vector<Rec> &v, size_t i) {
     return (int)(j - i);
 }
 
+// Whether a command before position i writes bytes of `st` (as an output or
+// as a written State input).
+static bool written_before(const std::vector<Rec> &v, size_t i, const slc_buffer_ref &st) {
+    for (size_t t = 0; t < i; t++) {
+        const Rec &r = v[t];
+        for (uint32_t o = 0; o < r.n_out; o++)
+            if (overlaps(r.out[o], st)) return true;
+        for (uint32_t q = 0; q < r.n_in; q++)
+            if (r.iv[q].role == SLC_ROLE_STATE && overlaps(r.in[q], st)) return true;
+    }
+    return false;
+}
+
+// Restores the programmatic-launch setting of this thread on scope exit.
+struct PdlScope {
+    bool saved = slc::k::pdl_enabled();
+    ~PdlScope() { slc::k::set_pdl_enabled(saved); }
+};
+
 // Runs the pending commands; dyn = kernels read the device scalar table
 // (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs;
 // the decode attention block (SplitHeads x3, Rope x2, CausalAttention,
@@ -222,7 +241,12 @@ static int matmul_run(const std::vector<Rec> &v, size_t i) {
 // Add followed by the RmsNorm of its sum as one launch.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     const std::vector<Rec> &v = cs->pending;
+    // The first command of a segment does not overlap earlier work: kernels
+    // that read data before their dependency wait can then only overlap
+    // commands of their own segment.
+    PdlScope pdl;
     for (size_t i = 0; i < v.size();) {
+        slc::k::set_pdl_enabled(pdl.saved && i > 0);
         if (v[i].op.code == SLC_OP_SPLIT_HEADS && i + 7 <= v.size() &&
             v[i + 5].op.code == SLC_OP_CAUSAL_ATTENTION) {
             BlockMember bm[7];
@@ -233,7 +257,8 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
             const Rec &at = v[i + 5];
             const uint32_t *ds = (dyn && at.slot >= 0) ? cs->d_table + at.slot : nullptr;
             bool launched = false;
-            int rc = slc_launch_attention_block(d, bm, ds, &launched);
+            const bool early = !written_before(v, i, at.in[3]);
+            int rc = slc_launch_attention_block(d, bm, ds, early, &launched);
             if (rc != SLC_OK) return rc;
             if (launched) {
                 i += 7;

@@ -105,8 +105,11 @@ struct BlockMember {
     const uint32_t *scalars;
     uint64_t n_scalars;
 };
+// early_cache: no command before the block in its segment writes the KV
+// state, so the attention kernel may read cached keys before its dependency
+// wait.
 int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
-                               bool *launched);
+                               bool early_cache, bool *launched);
 // Add(a, b) -> sum followed by RmsNorm(sum, w) -> out, both validated:
 // launched as one kernel when the shapes and buffer reuse allow it.
 int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMember *rms,

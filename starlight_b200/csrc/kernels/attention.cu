@@ -286,6 +286,7 @@ struct DecodeParams {
     float *cache;
     float *out;            // [B, H, 1, D]
     float *out2;           // optional second copy of out (merged heads, same layout at seq 1)
+    int early;             // cached keys may be read before the dependency wait
     float *part_o;         // [B * H][chunks][D]
     float *part_ml;        // [B * H][chunks][2]
     unsigned *tickets;     // [B * Hkv]
@@ -341,7 +342,6 @@ struct Vec<4> {
 template <int VEC, int G, int KPW>
 __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) {
     pdl_trigger();
-    pdl_wait();
     using V = Vec<VEC>;
     using T = typename V::T;
     constexpr int D = 32 * VEC;
@@ -352,6 +352,8 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int bh = blockIdx.y, chunk = blockIdx.x;
     const int b = bh / p.Hkv, kvh = bh - b * p.Hkv;
+    // past_len: a host scalar or the capture table (written by a copy ahead
+    // of the launch), never by a kernel.
     int past = p.past;
     if (p.d_past) {
         past = (int)*p.d_past;
@@ -363,6 +365,34 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     const int n_keys = past + 1;
     const int k0 = chunk * p.chunk_keys;
     const int k1 = min(n_keys, k0 + p.chunk_keys);
+    const float *kbase = p.cache + b * p.batch_stride + p.layer_off + (long long)kvh * D + lane * VEC;
+
+    // This warp's keys of one round (KPW keys kDecWarps apart), cached keys
+    // only; the new key (position past) comes from the inputs.
+    T kv[KPW], vv[KPW];
+    auto load_cached = [&](int j0) {
+#pragma unroll
+        for (int i = 0; i < KPW; i++) {
+            const int j = j0 + i * kDecWarps;
+            kv[i] = V::zero();
+            vv[i] = V::zero();
+            if (j < k1 && j != past) {
+                const float *src = kbase + (long long)j * p.time_stride;
+                kv[i] = V::ld(src);
+                vv[i] = V::ld(src + p.parity_stride);
+            }
+        }
+    };
+    int j0 = k0 + warp;
+    // With `early`, the first round's cached keys stream while the kernel
+    // producing q / k / v finishes (no command before it in its segment
+    // writes this cache).
+    bool loaded = false;
+    if (p.early && j0 < k1) {
+        load_cached(j0);
+        loaded = true;
+    }
+    pdl_wait();
 
     // Query rows of the group (lane slice), pre-scaled.
     T q[G];
@@ -382,18 +412,15 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         o[r] = V::zero();
     }
 
-    const float *kbase = p.cache + b * p.batch_stride + p.layer_off + (long long)kvh * D + lane * VEC;
     const float *knew = p.k_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
     const float *vnew = p.v_new + ((long long)b * p.Hkv + kvh) * D + lane * VEC;
-    for (int j0 = k0 + warp; j0 < k1; j0 += kDecWarps * KPW) {
-        // All of this warp's keys of the round in flight at once.
-        T kv[KPW], vv[KPW];
+    for (; j0 < k1; j0 += kDecWarps * KPW) {
+        if (!loaded) load_cached(j0);
+        loaded = false;
         int nk = 0;
 #pragma unroll
         for (int i = 0; i < KPW; i++) {
             const int j = j0 + i * kDecWarps;
-            kv[i] = V::zero();
-            vv[i] = V::zero();
             if (j < k1) {
                 nk = i + 1;
                 if (j == past) {
@@ -404,10 +431,6 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
                     float *dst = const_cast<float *>(kbase) + (long long)j * p.time_stride;
                     V::st(dst, kv[i]);
                     V::st(dst + p.parity_stride, vv[i]);
-                } else {
-                    const float *src = kbase + (long long)j * p.time_stride;
-                    kv[i] = V::ld(src);
-                    vv[i] = V::ld(src + p.parity_stride);
                 }
             }
         }
@@ -520,39 +543,50 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
         }
     }
     __syncthreads();
-    constexpr int kOut = (G * D + kDecThreads - 1) / kDecThreads;  // outputs per thread
-    constexpr int kBatch = 8;                                      // chunks per load batch
-    float acc[kOut];
+    // Each thread owns kU float4 outputs and keeps the partials of kB chunks
+    // in flight per batch; chunks are added in ascending order.
+    constexpr int kU = (G * D / 4 + kDecThreads - 1) / kDecThreads;
+    constexpr int kB = kU == 1 ? 16 : 8;
+    float4 acc[kU];
 #pragma unroll
-    for (int j = 0; j < kOut; j++) acc[j] = 0.f;
-    for (int c0 = 0; c0 < live; c0 += kBatch) {
-        float v[kBatch][kOut];
+    for (int j = 0; j < kU; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c0 = 0; c0 < live; c0 += kB) {
+        float4 v[kB][kU];
 #pragma unroll
-        for (int cc = 0; cc < kBatch; cc++)
+        for (int cc = 0; cc < kB; cc++)
 #pragma unroll
-            for (int j = 0; j < kOut; j++) {
-                const int idx = threadIdx.x + j * kDecThreads, c = c0 + cc;
-                const int r = idx / D, d = idx - r * D;
-                v[cc][j] = (idx < G * D && c < live)
-                               ? __ldcg(p.part_o + ((row0 + r) * p.chunks + c) * D + d)
-                               : 0.f;
+            for (int j = 0; j < kU; j++) {
+                const int u = threadIdx.x + j * kDecThreads, c = c0 + cc;
+                const int r = (4 * u) / D, d = 4 * u - r * D;
+                v[cc][j] = (u < G * D / 4 && c < live)
+                               ? __ldcg(reinterpret_cast<const float4 *>(
+                                     p.part_o + ((row0 + r) * p.chunks + c) * D + d))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
             }
 #pragma unroll
-        for (int cc = 0; cc < kBatch; cc++)
+        for (int cc = 0; cc < kB; cc++)
 #pragma unroll
-            for (int j = 0; j < kOut; j++) {
-                const int idx = threadIdx.x + j * kDecThreads, c = c0 + cc;
-                if (idx < G * D && c < live) acc[j] = fmaf(v[cc][j], sm_w[idx / D][c], acc[j]);
+            for (int j = 0; j < kU; j++) {
+                const int u = threadIdx.x + j * kDecThreads, c = c0 + cc;
+                if (u < G * D / 4 && c < live) {
+                    const float w = sm_w[(4 * u) / D][c];
+                    acc[j].x = fmaf(v[cc][j].x, w, acc[j].x);
+                    acc[j].y = fmaf(v[cc][j].y, w, acc[j].y);
+                    acc[j].z = fmaf(v[cc][j].z, w, acc[j].z);
+                    acc[j].w = fmaf(v[cc][j].w, w, acc[j].w);
+                }
             }
     }
 #pragma unroll
-    for (int j = 0; j < kOut; j++) {
-        const int idx = threadIdx.x + j * kDecThreads;
-        if (idx < G * D) {
-            const int r = idx / D, d = idx - r * D;
-            const float val = __fdiv_rn(acc[j], sm_inv[r]);
-            p.out[(row0 + r) * D + d] = val;
-            if (p.out2) p.out2[(row0 + r) * D + d] = val;
+    for (int j = 0; j < kU; j++) {
+        const int u = threadIdx.x + j * kDecThreads;
+        if (u < G * D / 4) {
+            const int r = (4 * u) / D, d = 4 * u - r * D;
+            const float inv = sm_inv[r];
+            const float4 val = make_float4(__fdiv_rn(acc[j].x, inv), __fdiv_rn(acc[j].y, inv),
+                                           __fdiv_rn(acc[j].z, inv), __fdiv_rn(acc[j].w, inv));
+            *reinterpret_cast<float4 *>(p.out + (row0 + r) * D + d) = val;
+            if (p.out2) *reinterpret_cast<float4 *>(p.out2 + (row0 + r) * D + d) = val;
         }
     }
     if (threadIdx.x == 0) p.tickets[bh] = 0u;  // ready for the next launch
@@ -632,17 +666,13 @@ __device__ __forceinline__ void rope_pair(const float *x, float *o, int base, in
 
 __global__ void __launch_bounds__(1024) decode_block_prep(const __grid_constant__ BlockPrep p) {
     pdl_trigger();
-    pdl_wait();
     extern __shared__ float sm[];
     const int D = p.D, half = D / 2;
     const int nq = p.B * p.H * D, nk = p.B * p.Hkv * D;
     float *q = sm, *k = q + nq, *v = k + nk, *trig = v + nk;  // trig [B][D]
     float *rq = trig + p.B * D, *rk = rq + nq;                  // roped q, k
-    for (int i = threadIdx.x; i < nq; i += blockDim.x) q[i] = p.q[i];
-    for (int i = threadIdx.x; i < nk; i += blockDim.x) {
-        k[i] = p.k[i];
-        v[i] = p.v[i];
-    }
+    // Positions are U32 data, written only by uploads (a U32 command output
+    // is illegal), so the f64 sine / cosine run before the dependency wait.
     for (int i = threadIdx.x; i < p.B * half; i += blockDim.x) {
         const int b = i / half, pr = i - b * half;
         const double angle = (double)p.pos[b] / p.denom[pr];
@@ -650,6 +680,12 @@ __global__ void __launch_bounds__(1024) decode_block_prep(const __grid_constant_
         sincos(angle, &sn, &cs);
         trig[b * D + pr] = (float)sn;
         trig[b * D + half + pr] = (float)cs;
+    }
+    pdl_wait();
+    for (int i = threadIdx.x; i < nq; i += blockDim.x) q[i] = p.q[i];
+    for (int i = threadIdx.x; i < nk; i += blockDim.x) {
+        k[i] = p.k[i];
+        v[i] = p.v[i];
     }
     __syncthreads();
     for (int i = threadIdx.x; i < p.B * p.H * half; i += blockDim.x) {
@@ -714,7 +750,7 @@ cudaError_t causal_attention_decode_into(cudaStream_t s, const float *q, const f
                                          const float *v, float *cache, float *out, float *out2,
                                          const KvGeometry &g, size_t heads, size_t past_len,
                                          float scale, const AttnScratch &scr,
-                                         const uint32_t *d_past) {
+                                         const uint32_t *d_past, bool early) {
     const size_t keys = d_past ? g.max_seq : past_len + 1;
     const size_t time_stride = g.kv_heads * g.head_dim;
     const size_t parity_stride = g.max_seq * time_stride;
@@ -729,6 +765,7 @@ cudaError_t causal_attention_decode_into(cudaStream_t s, const float *q, const f
     p.cache = cache;
     p.out = out;
     p.out2 = out2;
+    p.early = early ? 1 : 0;
     p.part_o = static_cast<float *>(scr.workspace);
     p.part_ml = p.part_o + g.batch * heads * dp.chunks * g.head_dim;
     p.tickets = scr.tickets;
@@ -781,7 +818,7 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
     DecodePlan dp = plan_decode(g.batch, g.kv_heads, heads, seq, g.head_dim, keys);
     if (dp.ok && g.batch * g.kv_heads <= scr.ticket_count)
         return causal_attention_decode_into(s, q, k, v, cache, out, nullptr, g, heads, past_len,
-                                            scale, scr, d_past);
+                                            scale, scr, d_past, false);
     cudaError_t e = kv_append(s, k, v, cache, g, past_len, seq, d_past);
     if (e != cudaSuccess) return e;
     Plan pl = plan(g.batch, heads, g.kv_heads, seq, keys - seq, g.head_dim);
@@ -842,7 +879,7 @@ bool decode_block_supported(size_t batch, size_t heads, size_t kv_heads, size_t 
 cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, float *cache,
                                    const KvGeometry &g, size_t heads, size_t past_len, float scale,
                                    float theta, int gptj, const AttnScratch &scr,
-                                   const uint32_t *d_past) {
+                                   const uint32_t *d_past, bool early_cache) {
     BlockPrep bp{};
     bp.q = io.q;
     bp.k = io.k;
@@ -876,7 +913,7 @@ cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, floa
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     return causal_attention_decode_into(s, bp.sq, bp.sk, bp.sv, cache, io.out, io.out_merged, g,
-                                        heads, past_len, scale, scr, d_past);
+                                        heads, past_len, scale, scr, d_past, early_cache);
 }
 
 }  // namespace k

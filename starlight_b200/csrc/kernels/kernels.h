@@ -83,7 +83,9 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
 
 // Decode (seq 1) attention block: SplitHeads q/k/v, Rope q/k, causal
 // attention with the KV append, MergeHeads, as two launches that leave every
-// output buffer as the seven commands would (attention.cu).
+// output buffer as the seven commands would (attention.cu). early_cache:
+// no kernel that may still run writes this KV cache, so its cached keys may
+// be read before the programmatic dependency wait.
 struct DecodeBlockIo {
     const float *q, *k, *v;  // [B, 1, H * D], [B, 1, Hkv * D] x 2
     const uint32_t *pos;     // [B, 1]
@@ -97,7 +99,7 @@ bool decode_block_supported(size_t batch, size_t heads, size_t kv_heads, size_t 
 cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, float *cache,
                                    const KvGeometry &g, size_t heads, size_t past_len, float scale,
                                    float theta, int gptj, const AttnScratch &scr,
-                                   const uint32_t *d_past);
+                                   const uint32_t *d_past, bool early_cache);
 
 // ---- matmul_f32.cu --------------------------------------------------------------
 // out[b] = a[b or 0] . w[b or 0]^T (NT) or a . w (NN), batch broadcast when a
@@ -165,6 +167,11 @@ cudaError_t rms_apply(cudaStream_t s, const float *x, const float *inv, const fl
 // out[i] = N(mean, std) draw number offset + i of the stream `seed`.
 cudaError_t fill_normal(cudaStream_t s, float *out, size_t n, uint64_t seed, uint64_t offset,
                         float mean, float std);
+
+// Whether launches on this thread may overlap their predecessor
+// (programmatic dependent launch; on by default).
+bool pdl_enabled();
+void set_pdl_enabled(bool on);
 
 // Launch counter (incremented by every launcher).
 uint64_t launch_count();

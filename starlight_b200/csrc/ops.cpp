@@ -692,7 +692,7 @@ bool disjoint(const slc_buffer_ref &a, const slc_buffer_ref &b) {
 }  // namespace
 
 int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
-                               bool *launched) {
+                               bool early_cache, bool *launched) {
     *launched = false;
     const BlockMember &sq = bm[0], &sk = bm[1], &sv = bm[2], &rq = bm[3], &rk = bm[4],
                       &at = bm[5], &mh = bm[6];
@@ -754,7 +754,8 @@ int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint3
                        kAttnTicketBytes / sizeof(unsigned), d->device_flag};
     cudaError_t e = k::decode_attention_block(d->stream, io, fp(at.in[3]), g, H, past,
                                               at.op->scale, rq.op->theta,
-                                              rq.op->rope_variant == SLC_ROPE_GPTJ, scr, dyn_past);
+                                              rq.op->rope_variant == SLC_ROPE_GPTJ, scr, dyn_past,
+                                              early_cache);
     if (e != cudaSuccess) return slc_fail(d, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
     *launched = true;
     return SLC_OK;
