@@ -42,7 +42,7 @@ PEAKS_PATH = os.path.join(ROOT, "MEASURED_PEAKS.json")
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tok/s (Llama-3-8B-shaped llama-dense, INT4 g128)"
 METRIC_70B = "decode tok/s (Llama-2-70B-shaped llama-dense, INT8 g128)"
-TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemv_int4_decode_8b.md")
+TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemv_imma_int4_28672x4096_m1.md")
 
 
 def parse_args(argv=None):
@@ -80,8 +80,8 @@ def hbm_peak():
 
 
 def profile_traffic_ratio():
-    """DRAM bytes / algorithmic bytes of the GEMV, from the committed ncu
-    summary of one full-size launch (profiles/gemv_int4_decode_8b.md)."""
+    """DRAM bytes / algorithmic bytes of the decode GEMV, from the committed
+    ncu summary of one full-size launch (the traffic_ratio line)."""
     try:
         for line in open(TRAFFIC_PROFILE):
             if line.strip().startswith("traffic_ratio:"):
@@ -351,7 +351,8 @@ def _gemv_roofline(dev, model, cfg, batch, peak):
     traffic = ratio * per_launch_bytes if ratio is not None else None
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0], "traffic": traffic,
-            "kernel": "qgemv_tma (quantized MatMulNT, M=%d) over one decode step's weight mix" % batch,
+            "kernel": ("quantized MatMulNT, M=%d (qgemv_lane / qgemv_imma) over one decode step's "
+                       "weight mix" % batch),
             "algorithmic_bytes_per_launch": per_launch_bytes, "launch_us": per_launch_s * 1e6,
             "peak_source": peak[1], "by_shape_NxK": shapes}
 

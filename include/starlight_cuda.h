@@ -179,7 +179,7 @@ typedef struct {
 
 typedef struct {
     /* Device scratch for split-K partial results, reserved once at creation
-     * because dispatch must not allocate. 0 selects the default (64 MiB). */
+     * because dispatch must not allocate. 0 selects the default (256 MiB). */
     uint64_t workspace_bytes;
     /* Host staging buffer (pinned) for upload/download. 0: default 16 MiB. */
     uint64_t staging_bytes;

@@ -31,7 +31,7 @@ using namespace slc;
 
 namespace {
 
-constexpr uint64_t kDefaultWorkspace = 64ull << 20;
+constexpr uint64_t kDefaultWorkspace = 256ull << 20;
 constexpr uint64_t kDefaultStaging = 16ull << 20;
 
 int set_error(slc_device *d, int status, const char *msg) {
