@@ -215,15 +215,21 @@ static int matmul_run(const std::vector<Rec> &v, size_t i) {
     return (int)(j - i);
 }
 
-// Whether a command before position i writes bytes of `st` (as an output or
-// as a written State input).
-static bool written_before(const std::vector<Rec> &v, size_t i, const slc_buffer_ref &st) {
+// Whether a command before position i writes bytes of layer `layer` of the
+// KV state `st`: as an output, or as the State input of an attention / append
+// command on the same layer (those write only their own layer's slice).
+static bool written_before(const std::vector<Rec> &v, size_t i, const slc_buffer_ref &st,
+                           uint32_t layer) {
     for (size_t t = 0; t < i; t++) {
         const Rec &r = v[t];
         for (uint32_t o = 0; o < r.n_out; o++)
             if (overlaps(r.out[o], st)) return true;
-        for (uint32_t q = 0; q < r.n_in; q++)
-            if (r.iv[q].role == SLC_ROLE_STATE && overlaps(r.in[q], st)) return true;
+        for (uint32_t q = 0; q < r.n_in; q++) {
+            if (r.iv[q].role != SLC_ROLE_STATE || !overlaps(r.in[q], st)) continue;
+            const bool layered = r.op.code == SLC_OP_CAUSAL_ATTENTION || r.op.code == SLC_OP_KV_APPEND;
+            if (!layered || r.op.layer == layer || memcmp(&r.in[q], &st, sizeof(st)) != 0)
+                return true;
+        }
     }
     return false;
 }
@@ -257,7 +263,7 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
             const Rec &at = v[i + 5];
             const uint32_t *ds = (dyn && at.slot >= 0) ? cs->d_table + at.slot : nullptr;
             bool launched = false;
-            const bool early = !written_before(v, i, at.in[3]);
+            const bool early = !written_before(v, i, at.in[3], at.op.layer);
             int rc = slc_launch_attention_block(d, bm, ds, early, &launched);
             if (rc != SLC_OK) return rc;
             if (launched) {

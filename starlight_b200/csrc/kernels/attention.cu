@@ -273,11 +273,11 @@ Plan plan(size_t batch, size_t heads, size_t kv_heads, size_t seq, size_t past_l
 
 // ---- decode -------------------------------------------------------------------
 
-constexpr int kDecThreads = 128;
+constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kDecMaxGroup = 8;
 constexpr int kDecKeysPerWarp = 4;  // keys in flight per warp
-constexpr int kDecMaxChunks = 256;  // chunks per (batch, kv_head)
+constexpr int kDecMaxChunks = 128;  // chunks per (batch, kv_head)
 
 struct DecodeParams {
     const float *q;        // [B, H, 1, D]
@@ -501,15 +501,18 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     if (p.chunks == 1) return;
 
     // Last CTA of this (batch, kv_head) merges the chunks in ascending order.
-    __threadfence();
+    // The barrier orders every thread's partial stores before thread 0's
+    // fence and ticket (release); its second fence orders the ticket before
+    // the barrier after which the last CTA reads the other partials.
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence();
         const unsigned ticket = atomicAdd(&p.tickets[bh], 1u);
         is_last = ticket == (unsigned)(p.chunks - 1);
+        __threadfence();
     }
     __syncthreads();
     if (!is_last) return;
-    __threadfence();
     // Chunk weights exp(m_c - M) per query row from statistics loaded in one
     // parallel pass; then every (row, dim) output adds the live chunks in
     // ascending order, its partial values loaded before the sum.
@@ -546,7 +549,7 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
     // Each thread owns kU float4 outputs and keeps the partials of kB chunks
     // in flight per batch; chunks are added in ascending order.
     constexpr int kU = (G * D / 4 + kDecThreads - 1) / kDecThreads;
-    constexpr int kB = kU == 1 ? 16 : 8;
+    constexpr int kB = kU == 1 ? 20 : 10;
     float4 acc[kU];
 #pragma unroll
     for (int j = 0; j < kU; j++) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -609,9 +612,10 @@ DecodePlan plan_decode(size_t batch, size_t kv_heads, size_t heads, size_t seq, 
         return pl;
     if (keys_max > (size_t)INT32_MAX || batch * kv_heads > 65535) return pl;
     const size_t bh = batch * kv_heads;
-    // About two CTAs per SM, each at least 32 keys.
-    size_t want = (2 * (size_t)kSmCount + bh - 1) / bh;
-    size_t by_len = (keys_max + 31) / 32;
+    // About one CTA per SM, each at least 64 keys (one round of its 8 warps),
+    // so that the last CTA merges few chunk partials.
+    size_t want = ((size_t)kSmCount + bh - 1) / bh;
+    size_t by_len = (keys_max + 63) / 64;
     size_t chunks = want < by_len ? want : by_len;
     if (chunks < 1) chunks = 1;
     size_t ck = (keys_max + chunks - 1) / chunks;
