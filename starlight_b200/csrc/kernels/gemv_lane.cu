@@ -457,8 +457,9 @@ LanePlan make_plan(const QuantSeg *segs, int nseg, size_t m) {
     const size_t gsteps = w0.group / kstep;
     // Launches of at most three tiles per SM, where the fixed cost of a
     // launch dominates; larger ones stream better through qgemv_imma's
-    // 128-row TMA boxes.
-    if ((gsteps & (gsteps - 1)) != 0 || tiles > 3LL * kSmCount) return pl;
+    // 128-row TMA boxes. Long rows (K > 8192) also go there: every CTA here
+    // stages the digits of all of K, qgemv_imma's only those of its K slice.
+    if ((gsteps & (gsteps - 1)) != 0 || tiles > 3LL * kSmCount || w0.k > 8192) return pl;
     pl.tiles = (int)tiles;
     pl.grid = (int)std::min<long long>(tiles, kSmCount);
     pl.spr = (int)(w0.row_bytes / 64);

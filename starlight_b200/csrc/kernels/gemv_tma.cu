@@ -702,18 +702,20 @@ __device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, i
                 frexpf(mx, &ex);
                 e = ex - 6;  // |x| < 2^ex, so |x / 2^e| < 64
             }
+            // Digits by exact power-of-two scaling (ldexpf outside the normal
+            // exponent range) and d = rint(y), y' = fma(d, -128, 128 y).
             int8_t *dst = xd + (3 * col) * p.Sn + st * WSB;
+            const bool direct = e >= -126 && e <= 126;
+            const float sc = __int_as_float((127 - e) << 23);
 #pragma unroll
             for (int i = 0; i < PER; i++) {
-                float d0 = 0.f, d1 = 0.f, d2 = 0.f;
-                if (!bad) {
-                    const float y = ldexpf(v[q][i], -e);
-                    d0 = rintf(y);
-                    float r = (y - d0) * 128.f;
-                    d1 = rintf(r);
-                    r = (r - d1) * 128.f;
-                    d2 = rintf(r);
-                }
+                float y = 0.f;
+                if (!bad) y = direct ? v[q][i] * sc : ldexpf(v[q][i], -e);
+                const float d0 = rintf(y);
+                const float r1 = fmaf(d0, -128.f, y * 128.f);
+                const float d1 = rintf(r1);
+                const float r2 = fmaf(d1, -128.f, r1 * 128.f);
+                const float d2 = rintf(r2);
                 const int off = imma_byte<FMT>(lane * PER + i);
                 dst[off] = (int8_t)(int)d0;
                 dst[p.Sn + off] = (int8_t)(int)d1;
