@@ -79,6 +79,15 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def bf16_peak():
+    """Measured dense bf16 burst peak (TFLOP/s) for the prefill GEMM fraction."""
+    try:
+        with open(PEAKS_PATH) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def profile_traffic_ratio():
     """DRAM bytes / algorithmic bytes of the decode GEMV, from the committed
     ncu summary of one full-size launch (the traffic_ratio line)."""
@@ -609,6 +618,7 @@ def run_sweep(args):
                 dev.release(extra)
 
     gemv, prefill = [], []
+    tc_peak = bf16_peak()
     for fmt in (QuantFormat.Int4, QuantFormat.Int8):
         for k, n in ((4096, 4096), (4096, 14336), (14336, 4096), (4096, 128256)):
             row_bytes = k // 2 if fmt == QuantFormat.Int4 else k
@@ -647,13 +657,17 @@ def run_sweep(args):
                 else:
                     flop = 2.0 * m * n * k
                     prefill.append({"fmt": fmt.name, "K": k, "N": n, "M": m, "us": round(us, 1),
-                                    "tflops": round(flop / us / 1e6, 2)})
+                                    "tflops": round(flop / us / 1e6, 2),
+                                    "frac": round(flop / us / 1e6 / tc_peak[0], 3)})
                 dev.release(xb)
                 dev.release(ob)
             for cb, sb in mats:
                 dev.release(cb)
                 dev.release(sb)
     emit({"sweep": "configs[1] ops, configs[2] quantized matmul", "hbm_peak_gbs": peak,
+          "bf16_peak_tflops": tc_peak[0], "peak_source": tc_peak[1],
+          "prefill_note": "frac = algorithmic 2MNK flops / measured bf16 burst peak; the tcgen05 "
+                          "GEMM executes twice that (bf16 hi + lo activation planes)",
           "timing": "CUDA-graph replay of one captured segment; inputs rotated over >= 2x L2",
           "ops": ops, "gemv": gemv, "prefill": prefill})
     dev.close()
