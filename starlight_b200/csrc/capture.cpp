@@ -243,8 +243,9 @@ struct PdlScope {
 // Runs the pending commands; dyn = kernels read the device scalar table
 // (graph capture). Runs of MatMulNT on one input go out as grouped GEMVs;
 // the decode attention block (SplitHeads x3, Rope x2, CausalAttention,
-// MergeHeads at seq 1) goes out as the fused two-launch block, and a residual
-// Add followed by the RmsNorm of its sum as one launch.
+// MergeHeads at seq 1) goes out as the fused two-launch block, a residual
+// Add followed by the RmsNorm of its sum as one launch, and a tensor-parallel
+// AllReduce feeding that pair as one peer-memory launch.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     const std::vector<Rec> &v = cs->pending;
     // The first command of a segment does not overlap earlier work: kernels
@@ -268,6 +269,21 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
             if (rc != SLC_OK) return rc;
             if (launched) {
                 i += 7;
+                continue;
+            }
+        }
+        if (v[i].op.code == SLC_OP_EXT_ALL_REDUCE && i + 2 < v.size() &&
+            v[i + 1].op.code == SLC_OP_ADD && v[i + 2].op.code == SLC_OP_RMS_NORM) {
+            BlockMember bm[3];
+            for (int t = 0; t < 3; t++) {
+                const Rec &r = v[i + t];
+                bm[t] = BlockMember{&r.op, r.in, r.iv, r.n_in, r.out, r.ov, r.scalars, r.n_scalars};
+            }
+            bool launched = false;
+            int rc = slc_launch_allreduce_add_rmsnorm(d, &bm[0], &bm[1], &bm[2], &launched);
+            if (rc != SLC_OK) return rc;
+            if (launched) {
+                i += 3;
                 continue;
             }
         }

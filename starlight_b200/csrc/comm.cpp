@@ -9,8 +9,16 @@
 // this is the Megatron-style tensor parallelism the llama-dense layer
 // admits: an all-reduce after the row-parallel o/down projections and an
 // all-gather of vocabulary-split logits.
+//
+// Peer exchange: for the decode-sized all-reduce (fused with the residual
+// Add and RmsNorm, comm_fused.cu) every rank allocates an exchange buffer at
+// init, shares its CUDA IPC handle through an NCCL all-gather and maps its
+// peers' buffers; the path is used only when every rank succeeded (agreed by
+// an NCCL min-reduction), otherwise the NCCL all-reduce serves all sizes.
+// SLC_PEER_ALLREDUCE=1 in the environment of every rank switches it on.
 #include <dlfcn.h>
 #include <nccl.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <mutex>
@@ -54,10 +62,106 @@ NcclApi &api() {
 
 }  // namespace
 
+// Exchange buffer geometry (rows x hidden per source rank and parity).
+constexpr size_t kXRows = 32, kXHidden = 8192;
+
 struct CommState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
+    bool peer_ok = false;
+    char *xbuf = nullptr;                        // this rank's exchange buffer
+    char *peer_base[slc::k::kMaxPeers] = {};     // every rank's buffer (own = xbuf)
+    size_t data_bytes = 0, flag_bytes = 0;
 };
+
+namespace {
+
+void release_peers(CommState *c) {
+    for (int p = 0; p < c->world && p < slc::k::kMaxPeers; p++)
+        if (p != c->rank && c->peer_base[p]) cudaIpcCloseMemHandle(c->peer_base[p]);
+    if (c->xbuf) cudaFree(c->xbuf);
+    for (auto &b : c->peer_base) b = nullptr;
+    c->xbuf = nullptr;
+    c->peer_ok = false;
+}
+
+bool peer_exchange_requested() {
+    const char *e = getenv("SLC_PEER_ALLREDUCE");
+    return e && strcmp(e, "1") == 0;
+}
+
+// Collective over all ranks: every rank calls it from slc_comm_init and takes
+// the same NCCL steps whatever fails (or is switched off) locally.
+void setup_peers(slc_device *d, CommState *c) {
+    NcclApi &a = api();
+    if (c->world < 2 || c->world > slc::k::kMaxPeers) return;
+    c->data_bytes = 2 * (size_t)c->world * kXRows * kXHidden * sizeof(float);
+    c->flag_bytes = 2 * (size_t)c->world * kXRows * sizeof(uint32_t);
+    const size_t total = c->data_bytes + c->flag_bytes + kXRows * sizeof(uint32_t);
+    bool ok = peer_exchange_requested() && cudaMalloc(&c->xbuf, total) == cudaSuccess &&
+              cudaMemset(c->xbuf, 0, total) == cudaSuccess &&
+              cudaDeviceSynchronize() == cudaSuccess;
+    cudaIpcMemHandle_t mine{};
+    if (ok) ok = cudaIpcGetMemHandle(&mine, c->xbuf) == cudaSuccess;
+    // Gather the handles through NCCL; staging in the kernel scratch.
+    char *dh = ws_scratch(d);
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    static_assert(sizeof(cudaIpcMemHandle_t) <= 64, "IPC handle size");
+    char handles[slc::k::kMaxPeers][64];
+    const bool gathered =
+        cudaMemcpyAsync(dh + (size_t)c->rank * 64, &mine, hb, cudaMemcpyHostToDevice, d->stream) ==
+            cudaSuccess &&
+        a.all_gather(dh + (size_t)c->rank * 64, dh, 64, ncclUint8, c->comm, d->stream) ==
+            ncclSuccess &&
+        cudaMemcpyAsync(handles, dh, 64 * (size_t)c->world, cudaMemcpyDeviceToHost, d->stream) ==
+            cudaSuccess &&
+        cudaStreamSynchronize(d->stream) == cudaSuccess;
+    ok = ok && gathered;
+    for (int p = 0; ok && p < c->world; p++) {
+        if (p == c->rank) {
+            c->peer_base[p] = c->xbuf;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, handles[p], hb);
+        void *ptr = nullptr;
+        ok = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+        c->peer_base[p] = static_cast<char *>(ptr);
+    }
+    cudaGetLastError();
+    // Agreement: on only if every rank succeeded.
+    int32_t flag = ok ? 1 : 0;
+    int32_t *df = reinterpret_cast<int32_t *>(dh);
+    const bool agreed =
+        cudaMemcpyAsync(df, &flag, 4, cudaMemcpyHostToDevice, d->stream) == cudaSuccess &&
+        a.all_reduce(df, df, 1, ncclInt32, ncclMin, c->comm, d->stream) == ncclSuccess &&
+        cudaMemcpyAsync(&flag, df, 4, cudaMemcpyDeviceToHost, d->stream) == cudaSuccess &&
+        cudaStreamSynchronize(d->stream) == cudaSuccess && flag == 1;
+    cudaGetLastError();
+    if (agreed)
+        c->peer_ok = true;
+    else
+        release_peers(c);
+}
+
+}  // namespace
+
+bool comm_peer_args(slc_device *d, slc::k::PeerReduceArgs *a) {
+    CommState *c = d ? d->comm : nullptr;
+    if (!c || !c->peer_ok) return false;
+    for (int p = 0; p < c->world; p++) {
+        a->peer_data[p] = reinterpret_cast<float *>(c->peer_base[p]);
+        a->peer_flags[p] = reinterpret_cast<uint32_t *>(c->peer_base[p] + c->data_bytes);
+    }
+    a->local_data = reinterpret_cast<const float *>(c->xbuf);
+    a->local_flags = reinterpret_cast<const uint32_t *>(c->xbuf + c->data_bytes);
+    a->counters = reinterpret_cast<uint32_t *>(c->xbuf + c->data_bytes + c->flag_bytes);
+    a->rank = c->rank;
+    a->world = c->world;
+    a->max_rows = kXRows;
+    a->max_hidden = kXHidden;
+    return true;
+}
 
 extern "C" int slc_comm_unique_id(uint8_t out_id[128]) {
     if (!out_id) return SLC_ERR_EXECUTION;
@@ -90,6 +194,7 @@ extern "C" int slc_comm_init(slc_device *d, const uint8_t unique_id[128], int ra
         return slc_fail(d, SLC_ERR_EXECUTION, "ncclCommInitRank failed");
     }
     d->comm = c;
+    setup_peers(d, c);
     return SLC_OK;
 }
 
@@ -102,6 +207,8 @@ extern "C" int slc_comm_world(const slc_device *d, int *rank, int *world) {
 
 void release_comm(slc_device *d) {
     if (!d->comm) return;
+    cudaSetDevice(d->ordinal);
+    release_peers(d->comm);
     if (d->comm->comm && api().ok) api().destroy(d->comm->comm);
     delete d->comm;
     d->comm = nullptr;

@@ -123,5 +123,12 @@ int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,
 
 // NCCL hooks (comm.cpp).
 void release_comm(slc_device *d);
+// Fills the peer-exchange fields of `a` (false when the communicator has no
+// peer exchange: world 1, switched off, or setup failed on some rank).
+bool comm_peer_args(slc_device *d, slc::k::PeerReduceArgs *a);
+// AllReduce(partial) -> Add(residual, partial) -> RmsNorm(sum), validated:
+// launched as the fused peer-memory kernel when its conditions hold.
+int slc_launch_allreduce_add_rmsnorm(slc_device *d, const BlockMember *ar, const BlockMember *add,
+                                     const BlockMember *rms, bool *launched);
 int comm_all_reduce(slc_device *d, float *data, uint64_t count);
 int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, uint64_t cols);

@@ -168,6 +168,31 @@ cudaError_t rms_apply(cudaStream_t s, const float *x, const float *inv, const fl
 cudaError_t fill_normal(cudaStream_t s, float *out, size_t n, uint64_t seed, uint64_t offset,
                         float mean, float std);
 
+// ---- comm_fused.cu ------------------------------------------------------------
+// Tensor-parallel all-reduce of `partial` over NVLink peer memory, fused with
+// the residual Add and RmsNorm that follow it (one CTA per row). The peer
+// exchange buffers are set up by the communicator (comm.cpp).
+constexpr int kMaxPeers = 8;
+struct PeerReduceArgs {
+    float *peer_data[kMaxPeers];       // data region of each rank's exchange buffer (mapped)
+    uint32_t *peer_flags[kMaxPeers];   // flag region of each rank's exchange buffer (mapped)
+    const float *local_data;           // this rank's data region
+    const uint32_t *local_flags;       // this rank's flag region
+    uint32_t *counters;                // [max_rows] call epochs, this rank
+    int rank, world;
+    size_t max_rows, max_hidden;
+    float *partial;                    // [rows, hidden]: partial in, rank-order sum out
+    const float *residual;             // [rows, hidden]
+    float *sum_out;                    // residual + sum
+    float *out;                        // rms_norm(sum_out) * weight
+    const float *weight;               // [hidden]
+    size_t rows, hidden;
+    float eps;
+    uint32_t *err;
+};
+bool allreduce_add_rms_supported(const PeerReduceArgs &a);
+cudaError_t allreduce_add_rms(cudaStream_t s, const PeerReduceArgs &a);
+
 // Whether launches on this thread may overlap their predecessor
 // (programmatic dependent launch; on by default).
 bool pdl_enabled();

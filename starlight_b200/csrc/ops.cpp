@@ -789,6 +789,56 @@ int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMem
     return SLC_OK;
 }
 
+int slc_launch_allreduce_add_rmsnorm(slc_device *d, const BlockMember *ar, const BlockMember *add,
+                                     const BlockMember *rms, bool *launched) {
+    *launched = false;
+    if (ar->op->code != SLC_OP_EXT_ALL_REDUCE || ar->n_in != 1 || add->op->code != SLC_OP_ADD ||
+        rms->op->code != SLC_OP_RMS_NORM || add->n_in != 2 || rms->n_in != 2 ||
+        !same_ref(rms->in[0], add->out[0]))
+        return SLC_OK;
+    // The all-reduced value is one of the Add's operands; the other is the
+    // residual.
+    int pi = -1;
+    if (same_ref(add->in[1], ar->in[0]))
+        pi = 1;
+    else if (same_ref(add->in[0], ar->in[0]))
+        pi = 0;
+    if (pi < 0) return SLC_OK;
+    const slc_value &xv = rms->iv[0];
+    if (xv.rank < 1 || xv.dtype != SLC_F32 || ar->iv[0].dtype != SLC_F32) return SLC_OK;
+    const uint64_t hidden = xv.dims[xv.rank - 1];
+    uint64_t rows = 1;
+    for (uint32_t r = 0; r + 1 < xv.rank; r++) rows *= xv.dims[r];
+    if (ar->in[0].len != rows * hidden || add->in[1 - pi].len != rows * hidden) return SLC_OK;
+    // Rows are read before the row's barrier and written after it; across
+    // rows the outputs may only reuse the inputs' bytes when there is a
+    // single row.
+    if (rows != 1 &&
+        (!disjoint(rms->out[0], add->in[0]) || !disjoint(rms->out[0], add->in[1]) ||
+         !disjoint(add->out[0], add->in[0]) || !disjoint(add->out[0], add->in[1]) ||
+         !disjoint(rms->out[0], add->out[0])))
+        return SLC_OK;
+    k::PeerReduceArgs a{};
+    if (!comm_peer_args(d, &a)) return SLC_OK;
+    auto fp = [&](const slc_buffer_ref &r) {
+        return reinterpret_cast<float *>(d->buffers[r.buffer].ptr) + r.offset;
+    };
+    a.partial = fp(ar->in[0]);
+    a.residual = fp(add->in[1 - pi]);
+    a.sum_out = fp(add->out[0]);
+    a.out = fp(rms->out[0]);
+    a.weight = fp(rms->in[1]);
+    a.rows = rows;
+    a.hidden = hidden;
+    a.eps = rms->op->eps;
+    a.err = d->device_flag;
+    if (!k::allreduce_add_rms_supported(a)) return SLC_OK;
+    if (k::allreduce_add_rms(d->stream, a) != cudaSuccess)
+        return slc_fail(d, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
+    *launched = true;
+    return SLC_OK;
+}
+
 int slc_launch_matmul_group(slc_device *d, const MatmulMember *mm, int n, bool *launched) {
     *launched = false;
     if (n < 2 || n > 4) return SLC_OK;

@@ -110,3 +110,109 @@ def test_tp2_logits_match_single_gpu(capture):
     for a, b in zip(tp, single):
         assert a.shape == b.shape
         assert_reduction(a.ravel(), b.ravel())
+
+
+# AllReduce(p) -> Add(x, p) -> RmsNorm: (rows, hidden, norm output reuses the
+# residual's bytes). The last case has more rows than the peer exchange holds.
+FUSED_CASES = [(1, 4096, True), (2, 512, False), (5, 1024, False), (3, 768, True),
+               (40, 256, False)]
+
+
+def _fused_expected_launches(rows, reuse):
+    if reuse and rows > 1:
+        return 3  # NCCL, Add, RmsNorm
+    return 1 if rows <= 32 else 2  # peer-memory kernel, or NCCL + fused Add/RmsNorm
+
+
+def _fused_rank(rank, world, port, q):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from oracle.pyoracle import Lcg
+    from starlight_b200.device import BufferRef, CudaDevice, Op, OpCode, Value, comm_unique_id
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["SLC_PEER_ALLREDUCE"] = "1"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120))
+    try:
+        dev = CudaDevice(rank)
+        t = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            t[:] = torch.frombuffer(bytearray(comm_unique_id()), dtype=torch.uint8)
+        dist.broadcast(t, 0)
+        dev.comm_init(bytes(t.numpy().tobytes()), rank, world)
+        F = Value.f32
+        bufs = []
+        for rows, hidden, reuse in FUSED_CASES:
+            n = rows * hidden
+            p0 = Lcg(100 * rows + hidden + rank).normal(n, 0.0, 1.0)
+            x0 = Lcg(7 * rows + hidden).normal(n, 0.0, 1.0)
+            w0 = Lcg(hidden).normal(hidden, 1.0, 0.1)
+            init = np.zeros(4 * n + hidden, np.float32)
+            init[:n], init[n:2 * n], init[4 * n:] = p0, x0, w0
+            bufs.append((dev.allocate_f32(init.size), init))
+
+        def run_case(ci):
+            rows, hidden, reuse = FUSED_CASES[ci]
+            n = rows * hidden
+            ar, init = bufs[ci]
+            dev.upload_f32(ar, init)
+            dev.synchronize()
+            p, x, s = BufferRef(ar, 0, n), BufferRef(ar, n, n), BufferRef(ar, 2 * n, n)
+            o = BufferRef(ar, n, n) if reuse else BufferRef(ar, 3 * n, n)
+            w = BufferRef(ar, 4 * n, hidden)
+            shape = (rows, hidden)
+            before = dev.launch_count()
+            dev.dispatch(Op(OpCode.AllReduce), [p], [F(shape)], [], [])
+            dev.dispatch(Op(OpCode.Add), [x, p], [F(shape), F(shape)], [s], [F(shape)])
+            dev.dispatch(Op(OpCode.RmsNorm, eps=1e-5), [s, w], [F(shape), F((hidden,))], [o],
+                         [F(shape)])
+            dev.synchronize()
+            launches = dev.launch_count() - before
+            return dev.download_f32(ar)[:4 * n], launches
+
+        eager = [run_case(ci) for ci in range(len(FUSED_CASES))]
+        dev.set_capture(True)
+        fused = [[run_case(ci) for ci in range(len(FUSED_CASES))] for _ in range(3)]
+        dev.close()
+        q.put((rank, eager, fused))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, repr(e), None))
+        raise
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_tp2_fused_allreduce_add_rms_norm_matches_commands():
+    # With capture on, the all-reduce and the Add + RmsNorm after it go out as
+    # one peer-memory kernel; at two ranks its rank-order sum equals NCCL's,
+    # so every byte (all-reduced partial, sum, normalised row) must equal the
+    # command-by-command run, on both ranks, over repeated calls (the kernel's
+    # per-row epochs and alternating slots).
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fused_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (e, f)) for r, e, f in (q.get(timeout=240) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    for r in range(2):
+        assert not isinstance(res[r][0], str), res[r][0]
+    assert all(p.exitcode == 0 for p in procs)
+    for r in range(2):
+        eager, fused = res[r]
+        for ci, (rows, hidden, reuse) in enumerate(FUSED_CASES):
+            np.testing.assert_array_equal(eager[ci][0], res[0][0][ci][0])
+            for rep in range(3):
+                got, launches = fused[rep][ci]
+                np.testing.assert_array_equal(got, eager[ci][0])
+                if rep > 0:
+                    assert launches == _fused_expected_launches(rows, reuse), (rows, reuse)
