@@ -15,7 +15,7 @@
 // init, shares its CUDA IPC handle through an NCCL all-gather and maps its
 // peers' buffers; the path is used only when every rank succeeded (agreed by
 // an NCCL min-reduction), otherwise the NCCL all-reduce serves all sizes.
-// SLC_PEER_ALLREDUCE=1 in the environment of every rank switches it on.
+// SLC_PEER_ALLREDUCE=0 in the environment of any rank switches it off.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <stdlib.h>
@@ -87,7 +87,7 @@ void release_peers(CommState *c) {
 
 bool peer_exchange_requested() {
     const char *e = getenv("SLC_PEER_ALLREDUCE");
-    return e && strcmp(e, "1") == 0;
+    return !(e && strcmp(e, "0") == 0);
 }
 
 // Collective over all ranks: every rank calls it from slc_comm_init and takes

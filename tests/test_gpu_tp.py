@@ -132,7 +132,6 @@ def _fused_rank(rank, world, port, q):
     from oracle.pyoracle import Lcg
     from starlight_b200.device import BufferRef, CudaDevice, Op, OpCode, Value, comm_unique_id
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    os.environ["SLC_PEER_ALLREDUCE"] = "1"
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
