@@ -612,9 +612,11 @@ DecodePlan plan_decode(size_t batch, size_t kv_heads, size_t heads, size_t seq, 
         return pl;
     if (keys_max > (size_t)INT32_MAX || batch * kv_heads > 65535) return pl;
     const size_t bh = batch * kv_heads;
-    // About one CTA per SM, each at least 64 keys (one round of its 8 warps),
-    // so that the last CTA merges few chunk partials.
-    size_t want = ((size_t)kSmCount + bh - 1) / bh;
+    // At most one CTA per SM (one wave: the kernel's registers allow one
+    // CTA per SM, so a 149th CTA would double the time), each at least 64
+    // keys (one round of its 8 warps), so that the last CTA merges few chunk
+    // partials.
+    size_t want = bh < (size_t)kSmCount ? (size_t)kSmCount / bh : 1;
     size_t by_len = (keys_max + 63) / 64;
     size_t chunks = want < by_len ? want : by_len;
     if (chunks < 1) chunks = 1;

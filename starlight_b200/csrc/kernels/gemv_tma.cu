@@ -107,6 +107,10 @@ struct TmaArgs {
     int Sn;                 // bytes per digit column (= 32 mod 128)
     int ncol;               // digit columns: 3 * M
     int xd_off, fx_off, red_off;  // shared offsets of digits, factors, block sums
+    // K slices (qgemv_imma): CTA c works on warp-steps [s * spr, (s + 1) * spr)
+    // of every row, s = c / (gridDim.x / nslice); spr, total and units then
+    // describe one slice. 1 everywhere else.
+    int nslice;
 };
 
 // Matrix of a (global) block and the block's index inside it.
@@ -351,7 +355,7 @@ __device__ __forceinline__ void stage_math(const TmaArgs &p, const unsigned char
 // g4 + 7, g4 rounded down to 4 groups = 16 bytes) into the next ring slot.
 __device__ __forceinline__ void produce(const TmaArgs &p, unsigned char *ring, uint64_t *full,
                                         uint64_t *empty, volatile int *abort, long long u0,
-                                        long long u1) {
+                                        long long u1, int kbase) {
     for (int i = 0; i < p.nseg; i++) {
         prefetch_tensormap(&p.codes_map[i]);
         prefetch_tensormap(&p.scales_map[i]);
@@ -367,7 +371,7 @@ __device__ __forceinline__ void produce(const TmaArgs &p, unsigned char *ring, u
         while (u < run_end) {
             const int run = (int)min((long long)kRun, run_end - u);
             if (!first_pass && !mbar_wait(&empty[slot], phase ^ 1, p.err, abort)) return;
-            const long long step0 = u - blk * p.spr;
+            const long long step0 = u - blk * p.spr + kbase;  // warp-step within the row
             const int g4 = (int)(step0 >> p.gs_shift) & ~3;
             unsigned char *sl = ring + slot * kSlotBytes;
             mbar_arrive_expect_tx(&full[slot], (uint32_t)kSlotBytes);
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     __syncthreads();
 
     if (warp == CW) {
-        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1);
+        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1, 0);
         return;
     }
 
@@ -628,7 +632,8 @@ __device__ __forceinline__ float i2f_small(int c) {
 // (INT4) or 2 (INT8) values; a warp issues the loads of up to kBatch blocks
 // before converting any, so staging costs about one load latency.
 template <int FMT, int CW, int NT>
-__device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, int nws) {
+__device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, int nws,
+                             int kbase) {
     constexpr int KSTEP = Fmt<FMT>::kStep;
     constexpr int PER = KSTEP / 32;
     constexpr int WSB = Imma<FMT>::kWsBytes;
@@ -645,7 +650,7 @@ __device__ void stage_digits(const TmaArgs &p, int8_t *xd, float *fx, int ws0, i
             const int col = b / nws;
             int st = ws0 + (b - col * nws);
             if (st >= spr) st -= spr;
-            const long long off = (long long)col * p.K + st * KSTEP + lane * PER;
+            const long long off = (long long)col * p.K + (long long)(kbase + st) * KSTEP + lane * PER;
             if constexpr (PER == 4) {
                 const float4 a = __ldg(reinterpret_cast<const float4 *>(p.x + off));
                 v[q][0] = a.x;
@@ -784,9 +789,11 @@ template <int FMT, int NT, int SPLIT, bool FULL>
 __device__ __forceinline__ void imma_stage(const TmaArgs &p, const unsigned char *base,
                                            const float *ssl, int step0, int run, int h,
                                            const unsigned char *xd, const float *fx, int g, int t,
-                                           float (&res)[NT][4]) {
+                                           int kbase, float (&res)[NT][4]) {
     constexpr int WSB = Imma<FMT>::kWsBytes;
-    const int g4 = (step0 >> p.gs_shift) & ~3;
+    // Digits and factors are indexed by the warp-step within the slice,
+    // scales by the warp-step within the row.
+    const int g4 = ((step0 + kbase) >> p.gs_shift) & ~3;
 #pragma unroll
     for (int jj = 0; jj < (kRun + SPLIT - 1) / SPLIT; jj++) {
         const int j = jj * SPLIT + h;
@@ -795,7 +802,7 @@ __device__ __forceinline__ void imma_stage(const TmaArgs &p, const unsigned char
             const int sw = step0 + j;
             imma_step<FMT, NT>(base + j * kStepBytes, kPitch, xd + sw * WSB + t * 8, p.Sn,
                                p.ncol, g, c);
-            const int gi = (sw >> p.gs_shift) - g4;
+            const int gi = ((sw + kbase) >> p.gs_shift) - g4;
             const float s0 = ssl[gi], s1 = ssl[8 * kScaleBox + gi];
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
@@ -829,7 +836,10 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     int *last_flag = reinterpret_cast<int *>(empty + kMaxStages);
     volatile int *abort = last_flag + 1;
 
-    const long long grid = gridDim.x, cta = blockIdx.x;
+    // This CTA's K slice and its index among the slice's CTAs.
+    const long long grid = gridDim.x / p.nslice;
+    const long long ks = blockIdx.x / grid, cta = blockIdx.x - ks * grid;
+    const int kbase = (int)(ks * p.spr);
     const long long u0 = unit_start(p, cta * p.units / grid);
     const long long u1 = unit_start(p, (cta + 1) * p.units / grid);
 
@@ -845,7 +855,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     __syncthreads();
 
     if (warp == CW) {
-        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1);
+        if (lane == 0) produce(p, ring, full, empty, abort, u0, u1, kbase);
         return;
     }
 
@@ -853,7 +863,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
     // Only the warp-steps this CTA's range touches (contiguous mod spr).
     const bool all_ws = u1 - u0 >= p.spr;
     stage_digits<FMT, CW, NT>(p, xd, fx, all_ws ? 0 : (int)(u0 % p.spr),
-                              all_ws ? (int)p.spr : (int)(u1 - u0));
+                              all_ws ? (int)p.spr : (int)(u1 - u0), kbase);
     float res[NT][4];
     int slot = 0, phase = 0;
     for (long long u = u0; u < u1;) {
@@ -880,11 +890,11 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
                 if (run == kRun)
                     imma_stage<FMT, NT, SPLIT, true>(p, base, ssl, step0, run, h,
                                                      reinterpret_cast<const unsigned char *>(xd),
-                                                     fx, g, t, res);
+                                                     fx, g, t, kbase, res);
                 else
                     imma_stage<FMT, NT, SPLIT, false>(p, base, ssl, step0, run, h,
                                                       reinterpret_cast<const unsigned char *>(xd),
-                                                      fx, g, t, res);
+                                                      fx, g, t, kbase, res);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -908,9 +918,12 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
             rw[(g + 8) * NC + c0 + 1] = res[nt][3];
         }
         consumer_sync<CW>();
+        // CTAs sharing the block: `shared` per K slice (the same in every
+        // slice); partial slots in slice order, then CTA order.
         const long long first = owner(p, blk * p.spr, grid);
         const long long last = owner(p, (blk + 1) * p.spr - 1, grid);
-        const int count = (int)(last - first + 1);
+        const int shared = (int)(last - first + 1);
+        const int count = shared * p.nslice;
         float *dst;
         long long ld, rbase;
         if (count == 1) {
@@ -918,7 +931,7 @@ __global__ void __launch_bounds__((kTiles * SPLIT + 1) * 32, 1)
             ld = n_seg;
             rbase = (long long)lblk * kBlockRows;
         } else {
-            dst = p.partials + (cta - first) * (long long)Mc * p.prow;
+            dst = p.partials + (ks * shared + (cta - first)) * (long long)Mc * p.prow;
             ld = p.prow;
             rbase = blk * kBlockRows;
         }
@@ -976,6 +989,9 @@ struct TmaPlan {
     bool imma = false;
     int int_nt = 0, int_nstage = 0, Sn = 0, xd_off = 0, fx_off = 0, red_off = 0;
     size_t int_smem = 0;
+    // K slices of the integer consumer (1: whole rows with the plan above).
+    int int_nslice = 1, int_grid = 0, int_slots = 0;
+    long long int_sps = 0;
 };
 
 constexpr int kImmaSplit = 2;  // consumer warps per 16-row tile in qgemv_imma
@@ -987,22 +1003,33 @@ int imma_nt(size_t m) {
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+constexpr int kMaxSlices = 64;  // at least two CTAs per slice
+
 // Shared layout of qgemv_imma: ring, digit planes [3M][Sn], factors
-// [spr][8 NT], block sums [warps][16][8 NT], barriers and flags.
+// [steps][8 NT], block sums [warps][16][8 NT], barriers and flags. The
+// digits of whole rows when they fit beside at least two stages; otherwise,
+// for at most 8 activation rows, the row is cut into 2, 4, .. 64 K slices
+// (each CTA stages the digits of one slice only, beside at least three
+// stages) and every slice's CTAs add partial sums. With more rows the slices
+// get so short that the per-block partial sums cost more than the weight
+// stream (70B-shaped batch-16 step 92 -> 130 ms when they were allowed).
 void plan_imma(TmaPlan &pl, int fmt, size_t m) {
     if (m > 16) return;
     const int nt = imma_nt(m);
     const long long wsb = fmt == 0 ? 128 : 64;
-    const long long sn = (long long)align_up((size_t)(pl.spr * wsb), 128) + 32;
-    const size_t xd = (size_t)(3 * m) * (size_t)sn;
-    const size_t fx = (size_t)pl.spr * 8 * nt * 4;
     const size_t red = (size_t)kTiles * kImmaSplit * 16 * 8 * nt * 4;
-    for (int ns = kMaxStages; ns >= 2; ns--) {
-        const size_t ring = (size_t)ns * kSlotBytes;
-        const size_t fx_off = align_up(ring + xd, 16);
-        const size_t red_off = align_up(fx_off + fx, 16);
-        const size_t total = red_off + red + 2 * kMaxStages * 8 + 16;
-        if (total <= (size_t)kSmemLimit) {
+    const int max_slices = nt <= 3 ? kMaxSlices : 1;
+    for (int nslice = 1; nslice <= max_slices && pl.spr % nslice == 0; nslice *= 2) {
+        const long long sps = pl.spr / nslice;
+        const long long sn = (long long)align_up((size_t)(sps * wsb), 128) + 32;
+        const size_t xd = (size_t)(3 * m) * (size_t)sn;
+        const size_t fx = (size_t)sps * 8 * nt * 4;
+        for (int ns = kMaxStages; ns >= (nslice == 1 ? 2 : kMinStages); ns--) {
+            const size_t ring = (size_t)ns * kSlotBytes;
+            const size_t fx_off = align_up(ring + xd, 16);
+            const size_t red_off = align_up(fx_off + fx, 16);
+            const size_t total = red_off + red + 2 * kMaxStages * 8 + 16;
+            if (total > (size_t)kSmemLimit) continue;
             pl.imma = true;
             pl.int_nt = nt;
             pl.int_nstage = ns;
@@ -1011,6 +1038,13 @@ void plan_imma(TmaPlan &pl, int fmt, size_t m) {
             pl.fx_off = (int)fx_off;
             pl.red_off = (int)red_off;
             pl.int_smem = total;
+            pl.int_nslice = nslice;
+            pl.int_sps = sps;
+            if (nslice > 1) {
+                const long long g = std::min<long long>(kSmCount / nslice, pl.n_blocks * sps);
+                pl.int_grid = (int)(g * nslice);
+                pl.int_slots = (int)(nslice * std::min<long long>(g, (g + pl.n_blocks - 1) / pl.n_blocks + 1));
+            }
             return;
         }
     }
@@ -1076,6 +1110,11 @@ TmaPlan make_tma_plan(const QuantSeg *segs, int nseg, size_t m) {
     pl.slots = pl.split == 1
                    ? 1
                    : (int)std::min<long long>(pl.grid, (pl.grid + n_blocks - 1) / n_blocks + 1);
+    if (pl.imma && pl.int_nslice == 1) {
+        pl.int_grid = pl.grid;
+        pl.int_slots = pl.slots;
+    }
+    if (pl.imma) pl.slots = std::max(pl.slots, pl.int_slots);
     pl.ok = true;
     return pl;
 }
@@ -1190,13 +1229,21 @@ cudaError_t launch_imma(cudaStream_t s, const float *x, const float *x2, size_t 
     a.xd_off = pl.xd_off;
     a.fx_off = pl.fx_off;
     a.red_off = pl.red_off;
+    a.nslice = pl.int_nslice;
+    if (pl.int_nslice > 1) {
+        // One slice's geometry: warp-steps as units.
+        a.spr = pl.int_sps;
+        a.total = pl.n_blocks * pl.int_sps;
+        a.units = a.total;
+        a.split = (int)pl.int_sps;
+    }
     static bool configured = false;
     if (!configured) {
         cudaFuncSetAttribute(qgemv_imma<FMT, NT, kImmaSplit>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         configured = true;
     }
-    launch_k(qgemv_imma<FMT, NT, kImmaSplit>, pl.grid, (kTiles * kImmaSplit + 1) * 32,
+    launch_k(qgemv_imma<FMT, NT, kImmaSplit>, pl.int_grid, (kTiles * kImmaSplit + 1) * 32,
              pl.int_smem, s, a);
     count_launch();
     return cudaGetLastError();

@@ -407,6 +407,18 @@ def test_quantized_matmul_irregular(dev, fmt, m, k, n, group):
     (32, 4096, 1024, 128),   # activation windows shorter than the row
     (17, 14336, 512, 128),   # three n-tiles, windows
     (5, 8192, 2064, 128),
+    (1, 4096, 16032, 128),   # 8-way TP vocabulary slice: many tiles, ragged last block
+    (1, 1792, 4096, 128),    # 8-way TP down projection K
+    # K slices (at most 8 rows): digits of whole rows do not fit beside the
+    # ring, so each CTA stages one slice and every slice's CTAs add partial sums
+    (8, 14336, 512, 128),
+    (8, 8192, 2064, 128),
+    (3, 14336, 1040, 128),
+    # more rows with long K: the other GEMV kernels
+    (16, 8192, 1024, 128),
+    (12, 8192, 2064, 128),
+    (16, 28672, 256, 128),   # 70B down projection at batch 16
+    (24, 4096, 1024, 128),
 ])
 def test_quantized_matmul_tma_shapes(dev, fmt, m, k, n, group):
     # The TMA-fed decode GEMV: ranges that split row blocks across CTAs
