@@ -689,6 +689,12 @@ bool same_ref(const slc_buffer_ref &a, const slc_buffer_ref &b) {
 bool disjoint(const slc_buffer_ref &a, const slc_buffer_ref &b) {
     return a.buffer != b.buffer || a.offset + a.len <= b.offset || b.offset + b.len <= a.offset;
 }
+// For kernels whose CTA reads a row of every input before a barrier and
+// writes the same row of every output after it: an output may take exactly
+// an input's bytes (every row then meets only itself), never a shifted range.
+bool row_safe(const slc_buffer_ref &out, const slc_buffer_ref &in) {
+    return disjoint(out, in) || same_ref(out, in);
+}
 }  // namespace
 
 int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint32_t *dyn_past,
@@ -773,9 +779,10 @@ int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMem
     uint64_t rows = 1;
     for (uint32_t r = 0; r + 1 < xv.rank; r++) rows *= xv.dims[r];
     // Rows are read before the barrier and written after it by the same
-    // CTA; across rows an output may only reuse the inputs' bytes when there
-    // is a single row.
-    if (rows != 1 && (!disjoint(rms->out[0], add->in[0]) || !disjoint(rms->out[0], add->in[1])))
+    // CTA; across rows an output may reuse an input's bytes only exactly.
+    if (rows != 1 && (!row_safe(rms->out[0], add->in[0]) || !row_safe(rms->out[0], add->in[1]) ||
+                      !row_safe(add->out[0], add->in[0]) || !row_safe(add->out[0], add->in[1]) ||
+                      !row_safe(rms->out[0], add->out[0])))
         return SLC_OK;
     auto fp = [&](const slc_buffer_ref &r) {
         return reinterpret_cast<float *>(d->buffers[r.buffer].ptr) + r.offset;

@@ -264,12 +264,12 @@ def test_fused_decode_attention_block_matches_commands(heads, kv_heads, head_dim
 
 
 @pytest.mark.parametrize("rows,hidden,reuse", [(1, 4096, True), (1, 256, True), (3, 4096, False),
-                                               (5, 1024, True)])
+                                               (5, 1024, True), (8, 4096, True)])
 def test_fused_add_rms_norm_matches_commands(rows, hidden, reuse):
     # Add(a, b) -> s then RmsNorm(s) -> o goes out as one launch with capture
-    # on. With reuse the norm's output takes the bytes of the dead addend a
-    # (fused only for a single row; otherwise the two commands run as such):
-    # every byte must equal command-by-command execution.
+    # on. With reuse the norm's output takes exactly the bytes of the dead
+    # addend a (each CTA reads its row before writing the same row): every
+    # byte must equal command-by-command execution.
     from starlight_b200.device import BufferRef
     lcg = Lcg(rows * 13 + hidden)
     n = rows * hidden
