@@ -434,30 +434,62 @@ __global__ void __launch_bounds__(kDecThreads) attention_decode(DecodeParams p) 
                 }
             }
         }
+        // Scores of the round: the lane's partial dots of every (row r, key
+        // i) pair, summed across the warp by a transposed butterfly (each
+        // stage hands half of the values a lane carries to its partner), so
+        // that lane holds the score of pair idx = lane / REP, idx = r KPW + i.
+        constexpr int NV = G * KPW, REP = 32 / NV;
+        constexpr int LOG = NV == 32 ? 5 : NV == 16 ? 4 : NV == 8 ? 3 : NV == 4 ? 2 : 1;
+        static_assert(NV <= 32 && 32 % NV == 0 && (1 << LOG) == NV, "pairs per round");
+        float v[NV];
+#pragma unroll
+        for (int r = 0; r < G; r++)
+#pragma unroll
+            for (int i = 0; i < KPW; i++) v[r * KPW + i] = V::dot(q[r], kv[i]);
+#pragma unroll
+        for (int st = 0; st < LOG; st++) {
+            const int half = NV >> (st + 1), sh = 16 >> st;
+            const bool upper = (lane & sh) != 0;
+#pragma unroll
+            for (int k2 = 0; k2 < half; k2++) {
+                const float send = upper ? v[k2] : v[k2 + half];
+                const float keep = upper ? v[k2 + half] : v[k2];
+                v[k2] = keep + __shfl_xor_sync(0xffffffffu, send, sh);
+            }
+        }
+#pragma unroll
+        for (int sh = REP / 2; sh >= 1; sh >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], sh);
+        const int idx = lane / REP, ri = idx / KPW, ii = idx - ri * KPW;
+        const float s = ii < nk ? v[0] : -INFINITY;
+        // Row maxima over the round's keys (KPW * REP aligned lanes per row).
+        float mb = s;
+#pragma unroll
+        for (int sh = KPW * REP / 2; sh >= 1; sh >>= 1)
+            mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, sh));
+        float m_new[G];
+        float m_own = 0.f;
 #pragma unroll
         for (int r = 0; r < G; r++) {
-            float sc[KPW];
-            float mb = -INFINITY;
+            m_new[r] = fmaxf(m[r], __shfl_sync(0xffffffffu, mb, r * KPW * REP));
+            if (r == ri) m_own = m_new[r];
+        }
+        const float p_own = s == -INFINITY ? 0.f : expf(s - m_own);
 #pragma unroll
-            for (int i = 0; i < KPW; i++) {
-                sc[i] = i < nk ? warp_sum(V::dot(q[r], kv[i])) : -INFINITY;
-                mb = fmaxf(mb, sc[i]);
-            }
-            const float m_new = fmaxf(m[r], mb);
-            const float alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new);
+        for (int r = 0; r < G; r++) {
+            const float alpha = m[r] == -INFINITY ? 0.f : expf(m[r] - m_new[r]);
             float lsum = l[r] * alpha;
             T acc = o[r];
 #pragma unroll
             for (int i = 0; i < VEC; i++) V::set(acc, i, V::get(acc, i) * alpha);
 #pragma unroll
             for (int i = 0; i < KPW; i++) {
-                const float pj = sc[i] == -INFINITY ? 0.f : expf(sc[i] - m_new);
+                const float pj = __shfl_sync(0xffffffffu, p_own, (r * KPW + i) * REP);
                 lsum += pj;
                 V::axpby(acc, 1.0f, pj, vv[i]);
             }
             o[r] = acc;
             l[r] = lsum;
-            m[r] = m_new;
+            m[r] = m_new[r];
         }
     }
 
