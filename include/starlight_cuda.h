@@ -294,22 +294,32 @@ int slc_comm_world(const slc_device *device, int *rank, int *world);
  * [m, n]; stream: a cudaStream_t (NULL = legacy default stream). The call is
  * asynchronous on that stream.
  *
- * Scratch: the split-K partial sums and tickets live in one fixed device
- * array of SLC_NOALLOC_SCRATCH_BYTES inside the library (on each device that
- * uses it). The tickets must start at zero: each call clears them on the
- * stream before its kernels. Problems whose scratch would exceed the array
- * (decode-sized m <= 64 with large n * split factor) are rejected with
- * SLC_ERR_OUT_OF_MEMORY and a message; m > 64 needs no scratch.
- * The first call on each device (with that device current) looks up the
- * array's device address; make that first call outside any stream capture.
- * Calls that overlap in time on one device (several streams or host threads)
- * share the array and race: serialize them, e.g. on one stream.
+ * Scratch: one fixed device array of SLC_NOALLOC_SCRATCH_BYTES inside the
+ * library (on each device that uses it). Decode-sized calls (m <= 64) keep
+ * the split-K tickets and partial sums there; prefill-sized calls (m > 64)
+ * keep the tcgen05 GEMM's bf16 hi/lo copies of x there, as many rows per
+ * pass as fit. The tickets must start at zero: each call clears them on the
+ * stream before its kernels. A decode-sized problem whose partial sums would
+ * exceed the array (large n times its split factor) is rejected with
+ * SLC_ERR_OUT_OF_MEMORY and a message rather than run on a slower GEMV that
+ * needs less scratch. The first call on each device (with that device
+ * current) looks up the array's device address; make that first call
+ * outside any stream capture. Every call, whatever its size, shares the
+ * array: calls that overlap in time on one device (several streams or host
+ * threads) race; serialize them, e.g. on one stream.
+ *
+ * error_word: device-accessible memory (device memory, or mapped pinned host
+ * memory) that a kernel sets to a nonzero code if one of its bounded waits
+ * gives up (the output is then incomplete). The library only ever sets it;
+ * the caller clears it and reads it after synchronizing the stream. NULL:
+ * such a failure is not reported.
  * Returns an slc_status; *error_message (if not NULL) is set to a static
  * string on failure. */
 #define SLC_NOALLOC_SCRATCH_BYTES (8u << 20)
 int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes, const float *scales,
                         uint64_t n, uint64_t k, uint32_t quant_format, uint32_t group_size,
-                        float *out, void *stream, const char **error_message);
+                        float *out, void *stream, uint32_t *error_word,
+                        const char **error_message);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -886,12 +886,8 @@ cudaError_t causal_attention(cudaStream_t s, const float *q, const float *k, con
     p.chunks = pl.chunks;
     p.scale = scale;
     p.d_past = d_past;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             227 * 1024);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(attention_kernel, 227 * 1024, &smem_set);
     dim3 grid((unsigned)pl.chunks, (unsigned)pl.grid_y, (unsigned)(g.batch * g.kv_heads));
     launch_k(attention_kernel, grid, kThreads, pl.smem, s, p);
     count_launch();
@@ -940,12 +936,8 @@ cudaError_t decode_attention_block(cudaStream_t s, const DecodeBlockIo &io, floa
     for (size_t pr = 0; pr < g.head_dim / 2; pr++)
         bp.denom[pr] = pow((double)theta, 2.0 * (double)pr / (double)g.head_dim);
     const size_t smem = block_prep_smem(g.batch, heads, g.kv_heads, g.head_dim);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(decode_block_prep, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             200 * 1024);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(decode_block_prep, 200 * 1024, &smem_set);
     launch_k(decode_block_prep, 1, 1024, smem, s, bp);
     count_launch();
     cudaError_t e = cudaGetLastError();

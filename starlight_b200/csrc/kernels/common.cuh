@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <utility>
 
 namespace slc {
@@ -93,6 +94,21 @@ cudaError_t launch_k(void (*kernel)(Params...), dim3 grid, dim3 block, size_t sm
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current
+// device, once per device. The attribute belongs to the device's context, so
+// `done` keeps one bit per device ordinal (ordinals >= 64 set it every call).
+template <typename Kernel>
+cudaError_t set_smem_limit_once(Kernel kernel, int bytes, std::atomic<uint64_t> *done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const uint64_t bit = dev >= 0 && dev < 64 ? (1ull << dev) : 0;
+    if (bit && (done->load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done->fetch_or(bit, std::memory_order_acq_rel);
+    return e;
 }
 
 // Host-side helpers.

@@ -522,12 +522,8 @@ cudaError_t launch_gemm(cudaStream_t s, const __nv_bfloat16 *hi, const __nv_bflo
     a.group = (int)w.group;
     a.groups = (int)w.groups;
     a.nst = (int)((w.k + BK - 1) / BK);
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(qgemm_tc_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg<FMT>::kSmem);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(qgemm_tc_kernel<FMT>, Cfg<FMT>::kSmem, &smem_set);
     dim3 grid((unsigned)((rows + BM - 1) / BM), (unsigned)((w.n + BN - 1) / BN));
     launch_k(qgemm_tc_kernel<FMT>, grid, kThreads, Cfg<FMT>::kSmem, s, a);
     count_launch();

@@ -549,12 +549,8 @@ cudaError_t launch_lane(cudaStream_t s, const float *x, const float *x2, size_t 
     a.ring_off = pl.ring_off;
     a.red_off = pl.red_off;
     a.bar_off = pl.bar_off;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(qgemv_lane<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemLimit);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(qgemv_lane<FMT>, kSmemLimit, &smem_set);
     launch_k(qgemv_lane<FMT>, pl.grid, kThreads, pl.smem, s, a);
     count_launch();
     return cudaGetLastError();

@@ -456,12 +456,8 @@ cudaError_t launch_fast(cudaStream_t s, const float *x, size_t m, const QuantWei
         a.tickets = static_cast<unsigned *>(ws);
         a.partials = reinterpret_cast<float *>(static_cast<char *>(ws) + 64 * 1024 * sizeof(unsigned));
     }
-    static bool configured[2][5] = {};
-    if (!configured[FMT][NT]) {
-        cudaFuncSetAttribute(qgemv_mma<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBudget);
-        configured[FMT][NT] = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(qgemv_mma<FMT, NT>, kSmemBudget, &smem_set);
     dim3 grid((unsigned)pl.row_blocks, (unsigned)pl.ksplit);
     launch_k(qgemv_mma<FMT, NT>, grid, kThreads, pl.smem, s, a);
     count_launch();

@@ -1206,12 +1206,8 @@ cudaError_t launch_tma(cudaStream_t s, const float *x, const float *x2, size_t m
                        uint32_t *err) {
     TmaArgs a{};
     if (!fill_args(a, FMT, x, x2, m, segs, nseg, pl, ws, err)) return cudaErrorInvalidValue;
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(qgemv_tma<FMT, NT, SPLIT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemLimit);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(qgemv_tma<FMT, NT, SPLIT>, kSmemLimit, &smem_set);
     launch_k(qgemv_tma<FMT, NT, SPLIT>, pl.grid, (kTiles * SPLIT + 1) * 32, pl.smem, s, a);
     count_launch();
     return cudaGetLastError();
@@ -1237,12 +1233,8 @@ cudaError_t launch_imma(cudaStream_t s, const float *x, const float *x2, size_t 
         a.units = a.total;
         a.split = (int)pl.int_sps;
     }
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(qgemv_imma<FMT, NT, kImmaSplit>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        configured = true;
-    }
+    static std::atomic<uint64_t> smem_set{0};
+    set_smem_limit_once(qgemv_imma<FMT, NT, kImmaSplit>, kSmemLimit, &smem_set);
     launch_k(qgemv_imma<FMT, NT, kImmaSplit>, pl.int_grid, (kTiles * kImmaSplit + 1) * 32,
              pl.int_smem, s, a);
     count_launch();

@@ -7,10 +7,13 @@
 // loop where cudaMalloc/cudaFree would block on or synchronize the device.
 // Such callers cannot create an slc_device either, because device creation
 // reserves a workspace. This entry point takes their device pointers and
-// stream directly and needs no allocation at all: the scratch memory of the
-// split-K GEMV (per-row-block tickets and partial sums) lives in a fixed
-// file-scope device array below, loaded with the library on every GPU that
-// uses it and kept until the process exits.
+// stream directly and needs no allocation at all: every scratch byte lives
+// in a fixed file-scope device array below, loaded with the library on every
+// GPU that uses it and kept until the process exits:
+//   [0, 256 KiB)   per-row-block tickets of the split-K decode GEMV;
+//   [256 KiB, 8 MiB)  the decode GEMV's partial sums (m <= 64), or the
+//                  tcgen05 prefill GEMM's bf16 hi/lo activation planes
+//                  (m > 64, rows processed in passes that fit).
 //
 // The computation is the one slc_dispatch(MatMulNT) performs on a
 // GroupwiseQuantized weight: the same launcher, plan and kernels.
@@ -44,7 +47,8 @@ int fail(const char **msg, int status, const char *text) {
 extern "C" int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes,
                                    const float *scales, uint64_t n, uint64_t k,
                                    uint32_t quant_format, uint32_t group_size, float *out,
-                                   void *stream, const char **error_message) {
+                                   void *stream, uint32_t *error_word,
+                                   const char **error_message) {
     if (error_message) *error_message = nullptr;
     if (quant_format != SLC_QUANT_INT4 && quant_format != SLC_QUANT_INT8)
         return fail(error_message, SLC_ERR_UNIMPLEMENTED, "unknown quantization format");
@@ -66,8 +70,11 @@ extern "C" int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes
     w.row_bytes = quant_format == SLC_QUANT_INT4 ? (k + 1) / 2 : k;
     w.format = (int)quant_format;
 
-    // Scratch this problem needs: the largest block of the decode path (rows
-    // are processed 32 at a time); prefill-sized m needs none.
+    // Split-K scratch of the decode path (rows go 32 at a time). The launcher
+    // itself would fall back to a slower GEMV that needs less scratch; this
+    // entry point rejects the problem instead, so that a caller never gets
+    // that slower path without knowing it. Prefill-sized m (> 64) always
+    // fits: the GEMM processes as many rows per pass as the array holds.
     size_t need = 0;
     if (m <= 64) {
         for (uint64_t m0 = 0; m0 < m; m0 += 32) {
@@ -103,13 +110,13 @@ extern "C" int slc_qmatmul_noalloc(const float *x, uint64_t m, const void *codes
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     // The tickets must start at zero; a previous call may have been cut short.
-    if (need > 0 && cudaMemsetAsync(scratch, 0, kTicketBytes, s) != cudaSuccess)
+    if (cudaMemsetAsync(scratch, 0, kTicketBytes, s) != cudaSuccess)
         return fail(error_message, SLC_ERR_EXECUTION, "clearing the scratch tickets failed");
     // The caller's stream may have just written the weights: no launch
     // overlap with the previous kernel.
     const bool pdl = slc::k::pdl_enabled();
     slc::k::set_pdl_enabled(false);
-    cudaError_t e = slc::k::qmatmul(s, x, m, w, out, scratch, kScratchBytes);
+    cudaError_t e = slc::k::qmatmul(s, x, m, w, out, scratch, kScratchBytes, error_word);
     slc::k::set_pdl_enabled(pdl);
     if (e != cudaSuccess) return fail(error_message, SLC_ERR_EXECUTION, "CUDA kernel launch failed");
     return SLC_OK;

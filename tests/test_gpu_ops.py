@@ -445,8 +445,11 @@ def test_quantized_matmul_prefill_tensor_cores(dev, fmt, m, k, n, group):
 
 
 @pytest.mark.parametrize("fmt,k,n", [(orc.INT4, 14336, 4096), (orc.INT4, 4096, 14336),
-                                     (orc.INT8, 8192, 1024)])
+                                     (orc.INT8, 8192, 1024), (orc.INT4, 4096, 128256),
+                                     (orc.INT8, 8192, 32000)])
 def test_quantized_matmul_full_size_spot_rows(dev, fmt, k, n):
+    # The last two are the 8B vocabulary projection (INT4) and the 70B one
+    # (INT8) at their full N.
     rows = np.array(sorted(set([0, 1, 15, 16, 127, 128, n // 2, n - 17, n - 1] +
                                list(Lcg(5).fill(32, 0, n - 1).astype(int)))))
     _qmatmul_case(dev, fmt, 1, k, n, 128, seed=k + n, spot_rows=rows)
