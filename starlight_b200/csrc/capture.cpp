@@ -93,6 +93,7 @@ static void drop_graphs(CaptureState *cs) {
 
 void invalidate_capture(slc_device *d) {
     if (d->capture) drop_graphs(d->capture);
+    decode_run_invalidate(d);
 }
 
 extern "C" int slc_set_capture(slc_device *d, int enabled) {
@@ -118,7 +119,7 @@ extern "C" int slc_set_capture(slc_device *d, int enabled) {
     cs->pending.reserve(1024);
     cs->key.reserve(1 << 20);
     d->capture = cs;
-    return SLC_OK;
+    return decode_run_create(d);
 }
 
 extern "C" int slc_capture_stats(const slc_device *d, slc_capture_info *out) {
@@ -133,6 +134,7 @@ void release_capture(slc_device *d) {
     cudaSetDevice(d->ordinal);
     cudaStreamSynchronize(d->stream);
     drop_graphs(cs);
+    decode_run_release(d);
     if (cs->h_table) cudaFreeHost(cs->h_table);
     if (cs->d_table) cudaFree(cs->d_table);
     if (cs->table_done) cudaEventDestroy(cs->table_done);
@@ -234,6 +236,44 @@ static bool written_before(const std::vector<Rec> &v, size_t i, const slc_buffer
     return false;
 }
 
+// BlockMember views of the recorded commands (the operator layer's form).
+static void members(const std::vector<Rec> &v, std::vector<BlockMember> *bm) {
+    bm->clear();
+    bm->reserve(v.size());
+    for (const Rec &r : v)
+        bm->push_back(BlockMember{&r.op, r.in, r.iv, r.n_in, r.out, r.ov, r.scalars, r.n_scalars});
+}
+
+// Runs of whole decoder layers that go out as one persistent launch:
+// (first command, command count), in order, non-overlapping.
+static std::vector<std::pair<size_t, size_t>> decode_runs(slc_device *d,
+                                                          const std::vector<BlockMember> &bm) {
+    std::vector<std::pair<size_t, size_t>> runs;
+    if (!d->decode) return runs;
+    for (size_t i = 0; i < bm.size();) {
+        const size_t n =
+            bm[i].op->code == SLC_OP_RMS_NORM ? decode_run_match(d, &bm[i], bm.size() - i) : 0;
+        if (n) {
+            runs.emplace_back(i, n);
+            i += n;
+        } else {
+            i++;
+        }
+    }
+    return runs;
+}
+
+// Device copies of the scalars of commands [first, first + n) (graph
+// capture), or null for commands without dynamic scalars.
+static std::vector<const uint32_t *> dyn_scalars(const CaptureState *cs, size_t first, size_t n) {
+    std::vector<const uint32_t *> out(n, nullptr);
+    for (size_t j = 0; j < n; j++) {
+        const Rec &r = cs->pending[first + j];
+        if (r.slot >= 0) out[j] = cs->d_table + r.slot;
+    }
+    return out;
+}
+
 // Restores the programmatic-launch setting of this thread on scope exit.
 struct PdlScope {
     bool saved = slc::k::pdl_enabled();
@@ -248,13 +288,31 @@ struct PdlScope {
 // AllReduce feeding that pair as one peer-memory launch.
 static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     const std::vector<Rec> &v = cs->pending;
+    std::vector<BlockMember> all;
+    members(v, &all);
+    const auto runs = decode_runs(d, all);
+    size_t next_run = 0;
     // The first command of a segment does not overlap earlier work: kernels
     // that read data before their dependency wait can then only overlap
     // commands of their own segment.
     PdlScope pdl;
     for (size_t i = 0; i < v.size();) {
         slc::k::set_pdl_enabled(pdl.saved && i > 0);
-        if (v[i].op.code == SLC_OP_SPLIT_HEADS && i + 7 <= v.size() &&
+        if (next_run < runs.size() && runs[next_run].first == i) {
+            const size_t n = runs[next_run].second;
+            next_run++;
+            const auto ds = dyn_scalars(cs, i, n);
+            bool launched = false;
+            int rc = decode_run_launch(d, &all[i], n, dyn ? ds.data() : nullptr, false, &launched);
+            if (rc != SLC_OK) return rc;
+            if (launched) {
+                i += n;
+                continue;
+            }
+        }
+        // Other fusions end before the next decode run begins.
+        const size_t limit = next_run < runs.size() ? runs[next_run].first : v.size();
+        if (v[i].op.code == SLC_OP_SPLIT_HEADS && i + 7 <= limit &&
             v[i + 5].op.code == SLC_OP_CAUSAL_ATTENTION) {
             BlockMember bm[7];
             for (int t = 0; t < 7; t++) {
@@ -272,7 +330,7 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
                 continue;
             }
         }
-        if (v[i].op.code == SLC_OP_EXT_ALL_REDUCE && i + 2 < v.size() &&
+        if (v[i].op.code == SLC_OP_EXT_ALL_REDUCE && i + 3 <= limit &&
             v[i + 1].op.code == SLC_OP_ADD && v[i + 2].op.code == SLC_OP_RMS_NORM) {
             BlockMember bm[3];
             for (int t = 0; t < 3; t++) {
@@ -287,7 +345,7 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
                 continue;
             }
         }
-        if (v[i].op.code == SLC_OP_ADD && i + 1 < v.size() &&
+        if (v[i].op.code == SLC_OP_ADD && i + 2 <= limit &&
             v[i + 1].op.code == SLC_OP_RMS_NORM) {
             const Rec &ra = v[i], &rr = v[i + 1];
             const BlockMember add{&ra.op, ra.in, ra.iv, ra.n_in, ra.out, ra.ov, ra.scalars,
@@ -302,7 +360,7 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
                 continue;
             }
         }
-        const int run = matmul_run(v, i);
+        const int run = (int)std::min<size_t>((size_t)matmul_run(v, i), limit - i);
         if (run > 1) {
             MatmulMember mm[4];
             for (int t = 0; t < run; t++)
@@ -343,6 +401,19 @@ static int upload_table(slc_device *d, CaptureState *cs) {
 }
 
 static bool try_capture(slc_device *d, CaptureState *cs, Graph *g) {
+    // Program images of decode runs are uploaded now: nothing may be copied
+    // to the device while the stream is being captured.
+    if (d->decode) {
+        std::vector<BlockMember> all;
+        members(cs->pending, &all);
+        for (const auto &run : decode_runs(d, all)) {
+            const auto ds = dyn_scalars(cs, run.first, run.second);
+            bool launched = false;
+            if (decode_run_launch(d, &all[run.first], run.second, ds.data(), true, &launched) !=
+                SLC_OK)
+                d->last = slc_error{};
+        }
+    }
     const uint64_t before = slc::k::launch_count();
     if (cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
         cudaGetLastError();

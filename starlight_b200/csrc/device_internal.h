@@ -25,6 +25,7 @@ struct QuantBinding {
 
 struct CaptureState;  // command capture and graph replay (capture.cpp)
 struct CommState;     // NCCL communicator (comm.cpp)
+struct DecodeRunState;  // persistent decode-layer fusion (decode_run.cpp)
 
 struct slc_device {
     int ordinal = 0;
@@ -40,6 +41,7 @@ struct slc_device {
     slc_error last{};
     CaptureState *capture = nullptr;
     CommState *comm = nullptr;
+    DecodeRunState *decode = nullptr;
 };
 
 // Device workspace layout (reserved once at creation; dispatch never
@@ -132,3 +134,17 @@ int slc_launch_allreduce_add_rmsnorm(slc_device *d, const BlockMember *ar, const
                                      const BlockMember *rms, bool *launched);
 int comm_all_reduce(slc_device *d, float *data, uint64_t count);
 int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, uint64_t cols);
+
+// Persistent decode-layer fusion (decode_run.cpp), created with capture.
+int decode_run_create(slc_device *d);
+void decode_run_release(slc_device *d);
+// Drops the program images of captured graphs (with the graphs).
+void decode_run_invalidate(slc_device *d);
+// Commands at the start of cmds[0..n) that form whole decoder layers the
+// persistent kernel can run (0: none).
+size_t decode_run_match(slc_device *d, const BlockMember *cmds, size_t n);
+// Launches the matched run cmds[0..n) (n from decode_run_match). dyn: device
+// copies of each command's scalars (graph capture) or null. prepare_only:
+// upload a graph's program image before its capture begins, launch nothing.
+int decode_run_launch(slc_device *d, const BlockMember *cmds, size_t n, const uint32_t *const *dyn,
+                      bool prepare_only, bool *launched);

@@ -193,6 +193,50 @@ struct PeerReduceArgs {
 bool allreduce_add_rms_supported(const PeerReduceArgs &a);
 cudaError_t allreduce_add_rms(cudaStream_t s, const PeerReduceArgs &a);
 
+// ---- decode_layers.cu ------------------------------------------------------------
+// Persistent decode of a run of llama-dense layers at batch 1 (one
+// cooperative launch; see decode_layers.cu). Outputs of a layer's sixteen
+// commands, in command order:
+//   RmsNorm h, MatMulNT q k v, SplitHeads qs ks vs, Rope qr kr,
+//   CausalAttention a, MergeHeads am, MatMulNT o, Add x1, RmsNorm h2,
+//   SwiGlu f, Add xn.
+constexpr int kDlCmds = 16;
+enum DlCmd {
+    kDlH = 0, kDlQ, kDlK, kDlV, kDlQs, kDlKs, kDlVs, kDlQr, kDlKr, kDlA, kDlAm, kDlO, kDlX1,
+    kDlH2, kDlF, kDlXn
+};
+struct DlLayerIo {
+    QuantWeight w[7];          // q, k, v, o, gate, up, down
+    const float *wn1, *wn2;    // attention / MLP RmsNorm weights
+    float eps1, eps2, scale;   // RmsNorm eps, attention scale
+    uint32_t cache_layer;      // the CausalAttention's layer attribute
+    uint32_t past;             // host past_len (eager)
+    const uint32_t *d_past;    // device past_len (graph replay) or null
+    float *cmd[kDlCmds];       // command output buffers
+};
+struct DlRun {
+    uint32_t layers, hidden, heads, kv_heads, head_dim, inter;
+    int format;                // 0 INT4, 1 INT8
+    uint32_t group;
+    int gptj;
+    float theta;
+    const float *x0;           // input of the first layer's RmsNorm
+    const uint32_t *pos;       // [1] position of the decode token
+    float *cache;              // KV state [1, cache_layers, 2, max_seq, kv_heads, head_dim]
+    uint32_t cache_layers, max_seq;
+    const DlLayerIo *layer;    // [layers]
+};
+bool decode_layers_supported(const DlRun &r);
+size_t decode_layers_image_bytes(int layers);
+size_t decode_layers_scratch_bytes(const DlRun &r);
+// Writes the run's program image (TMA tensor maps of every weight and the
+// layer table) into host memory; the caller copies it to dev_image.
+bool decode_layers_image(const DlRun &r, void *host_image, size_t bytes, const void *dev_image);
+// sync: zeroed device words (kDecodeSyncWords), left zeroed by the kernel.
+constexpr int kDecodeSyncWords = 2048;
+cudaError_t decode_layers(cudaStream_t s, const DlRun &r, const void *dev_image, void *scratch,
+                          size_t scratch_bytes, unsigned *sync, uint32_t *err);
+
 // Whether launches on this thread may overlap their predecessor
 // (programmatic dependent launch; on by default).
 bool pdl_enabled();

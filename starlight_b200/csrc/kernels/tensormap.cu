@@ -55,5 +55,19 @@ bool encode_tensor_map(CUtensorMap *map, CUtensorMapDataType dtype, const void *
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+bool encode_tensor_map_3d(CUtensorMap *map, CUtensorMapDataType dtype, const void *base,
+                          const uint64_t dims[3], const uint64_t strides_bytes[2],
+                          const uint32_t box[3]) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    const cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+    const cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, dtype, 3, const_cast<void *>(base), d, st, bx, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace k
 }  // namespace slc

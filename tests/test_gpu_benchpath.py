@@ -45,6 +45,7 @@ def test_benchmark_shape_with_capture_matches_oracle(batch, prefill, steps):
     ref = orc.Llama(ocfg)
     ref.init_random(2024, 0.02)
     dev = CudaDevice(0)
+    model = None
     try:
         dev.set_capture(True)
         model = Llama(dev, cfg)
@@ -71,6 +72,7 @@ def test_benchmark_shape_with_capture_matches_oracle(batch, prefill, steps):
         stats = dev.capture_stats()
         # Decode steps 3.. replay one captured graph each.
         assert stats["replays"] >= steps - 2, stats
-        model.close()
     finally:
+        if model is not None:  # the model refers to the device: close it first
+            model.close()
         dev.close()
