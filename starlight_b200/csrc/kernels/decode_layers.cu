@@ -52,15 +52,21 @@
 // GEMV (the decode GEMV arithmetic of gemv_lane.cu): weights in 16-row
 // tiles; each worker owns a contiguous range of whole tiles (no cross-CTA
 // sums). A tile is streamed in chunks of [16 rows][1 KiB of codes] (one 2-D
-// TMA box of 1 KiB rows) plus the chunk's scales ([16 rows][groups of the
-// chunk], a second box); consumer warp w multiplies the 64-byte warp-step w
-// of every chunk with the s8 tensor-core path (INT4 nibbles as 16 x code,
-// activations as three exact 7-bit digits per value in the MMA's N
-// dimension, integer block sums converted exactly and scaled by
-// scale * 2^e * 2^-7d). Warp sums of every tile are added in warp order.
+// TMA box, rows padded in shared memory so that neighbouring rows sit 16
+// banks apart) plus the chunk's scales ([16 rows][groups of the chunk], a
+// second box, padded likewise); a worker's tiles go in groups of four,
+// chunk by chunk within a group. Consumer warp w multiplies the 64-byte
+// warp-steps 2w and 2w + 1 of every chunk with the s8 tensor-core path
+// (INT4 nibbles as 16 x code, activations as three exact 7-bit digits per
+// value in the MMA's N dimension, integer block sums converted exactly and
+// scaled by scale * 2^e * 2^-7d), reusing a chunk's digits for the whole
+// group. Warp sums of every tile are added in warp order.
 //
 // HBM traffic per layer: the quantized weights (codes + scales) once, the
-// KV cache rows [0, past) of the layer once, plus activations (KBs).
+// KV cache rows [0, past) of the layer once, plus activations (KBs). The
+// padding boxes also read the first 64 code bytes (16 scale bytes) of the
+// row's next chunk, which the next box of the same tile reads again from
+// L2; past a row's end they are zero fill.
 //
 // Every wait is bounded (1 s): a CTA that gives up records kErrWaitTimeout,
 // raises the global abort word (every other CTA then stops waiting at its
@@ -90,12 +96,27 @@ constexpr int kCons = 8;                     // consumer warps (each takes two w
                                              // of every chunk; 9 warps leave 168 registers
                                              // a thread, so nothing spills to local memory)
 constexpr int kConsThreads = kCons * 32;
-constexpr int kThreads = kConsThreads + 32;  // + producer warp
+// + the producer warpgroup: one warp (lane 0) walks the weights, three stay
+// idle. At the start the producer warpgroup lowers its registers to
+// kProdRegs and the consumer warpgroups raise theirs to kConsRegs
+// (setmaxnreg); the block is launched with 168 a thread, and
+// 384 x 168 = 256 x kConsRegs + 128 x kProdRegs, so the raise never waits
+// for registers that do not exist.
+constexpr int kThreads = kConsThreads + 128;
+constexpr int kLaunchRegs = 168, kConsRegs = 224, kProdRegs = 56;
+static_assert(kThreads * kLaunchRegs == kConsThreads * kConsRegs + 128 * kProdRegs,
+              "register split");
 constexpr int kSlots = 8;                    // ring slots
 constexpr int kChunk = 1024;                 // code bytes per row per chunk
-constexpr int kSlotCode = 16 * kChunk;       // 16 rows of codes (or 16 K + 16 V rows)
-constexpr int kSlotBytes = kSlotCode + 1024; // + scales [16 rows][<= 16 groups]
-constexpr int kRedTiles = 4;                 // tiles per cross-warp reduction
+// A slot holds 16 rows of a chunk; each row is followed by 64 bytes (the
+// start of the next chunk, or the zero fill past the row's end) so that
+// rows r and r + 1 start 16 banks apart and a quarter-warp's 16-byte loads
+// of two rows never share a bank.
+constexpr int kRowPad = 64;
+constexpr int kSlotCode = 16 * (kChunk + kRowPad);  // codes (or 16 K + 16 V rows)
+constexpr int kScalePad = 4;                 // floats after each row's chunk scales
+constexpr int kSlotBytes = kSlotCode + 16 * (16 + kScalePad) * 4;  // + scales [16][<= 20]
+constexpr int kRedTiles = 4;                 // tiles per group (one cross-warp reduction)
 constexpr int kD = 128;                      // head_dim
 constexpr int kMaxLayers = 128;
 constexpr int kSmemLimit = 227 * 1024;
@@ -301,7 +322,18 @@ struct StageGeo {
     int tend0, tend1;        // cumulative 16-row tiles of the first two
     float *out0, *out1, *out2;  // private outputs
     int tiles, K, rowb, C, nch, wact, gpc;
+    int Cp, gps;  // slot row strides: code bytes, scale floats
 };
+
+// Slot row strides of a stage with rows of rowb code bytes in chunks of C
+// bytes holding gpc scale groups (the boxes the host encodes match).
+// Single-chunk rows are copied unpadded (the box never exceeds the row).
+__host__ __device__ __forceinline__ int slot_code_stride(int rowb, int C) {
+    return (rowb > C && C % 128 == 0) ? C + kRowPad : C;
+}
+__host__ __device__ __forceinline__ int slot_scale_stride(int rowb, int C, int gpc) {
+    return rowb > C ? gpc + kScalePad : gpc;
+}
 
 template <int FMT>
 __device__ __forceinline__ StageGeo stage_geo(const DlArgs &p, int st) {
@@ -341,6 +373,8 @@ __device__ __forceinline__ StageGeo stage_geo(const DlArgs &p, int st) {
     g.nch = g.rowb / g.C;
     g.wact = g.C / 64;
     g.gpc = g.C * (FMT == 0 ? 2 : 1) / p.group;
+    g.Cp = slot_code_stride(g.rowb, g.C);
+    g.gps = slot_scale_stride(g.rowb, g.C, g.gpc);
     return g;
 }
 
@@ -443,20 +477,25 @@ __device__ void producer(const DlArgs &p, const Smem sm) {
                 }
                 continue;
             }
+            // This worker's tiles in groups of kRedTiles, each group chunk by
+            // chunk (the consumers reuse a chunk's digits across the group).
             const StageGeo g = stage_geo<FMT>(p, st);
             const int t0 = (int)((long long)c * g.tiles / W);
             const int t1 = (int)((long long)(c + 1) * g.tiles / W);
-            for (int t = t0; t < t1 && !stop; t++) {
-                int row;
-                const int m = tile_mat(g, t, &row);
-                const CUtensorMap *cm = maps + ly.map[stage_mat(g, m)];
-                const uint32_t bytes = (uint32_t)(16 * g.C + 16 * g.gpc * 4);
-                for (int ch = 0; ch < g.nch; ch++) {
-                    unsigned char *dst = next_slot(bytes);
-                    if (!dst) break;
-                    uint64_t *bar = &sm.full[(seq - 1) % kSlots];
-                    tma_load_2d(dst, cm, ch * (g.C / 4), row, bar, pol);
-                    tma_load_2d(dst + kSlotCode, cm + 1, ch * g.gpc, row, bar, pol);
+            const uint32_t bytes = (uint32_t)(16 * g.Cp + 16 * g.gps * 4);
+            for (int tg = t0; tg < t1 && !stop; tg += kRedTiles) {
+                const int nb = min(kRedTiles, t1 - tg);
+                for (int ch = 0; ch < g.nch && !stop; ch++) {
+                    for (int b = 0; b < nb; b++) {
+                        int row;
+                        const int m = tile_mat(g, tg + b, &row);
+                        const CUtensorMap *cm = maps + ly.map[stage_mat(g, m)];
+                        unsigned char *dst = next_slot(bytes);
+                        if (!dst) break;
+                        uint64_t *bar = &sm.full[(seq - 1) % kSlots];
+                        tma_load_2d(dst, cm, ch * (g.C / 8), row, bar, pol);  // u64 units
+                        tma_load_2d(dst + kSlotCode, cm + 1, ch * g.gpc, row, bar, pol);
+                    }
                 }
             }
         }
@@ -636,94 +675,73 @@ __device__ __forceinline__ void fetch_digits(const DlArgs &p, const Smem &sm,
 }
 
 // ---- consumers: GEMV over this worker's tiles -----------------------------------
+//
+// Warp w multiplies the adjacent warp-steps 2w and 2w + 1 (64 code bytes each)
+// of every chunk. A worker's tiles are streamed in groups of kRedTiles tiles,
+// chunk by chunk within a group, so a warp loads a chunk's digit fragments
+// and factors once and uses them for every tile of the group; each tile
+// keeps its own row sums in registers (chunks added in ascending order).
 
-// One warp-step (16 rows x 64 bytes of codes) of a landed chunk: the s8
-// tensor-core product with the warp's staged digits, scaled and added to
-// the warp's row sums.
+// The digit fragments (B operands) and factors of warp-steps ws0 and ws0 + 1
+// of the stage input, from the shared digit vector.
 template <int FMT>
-__device__ __forceinline__ void gemv_item(const unsigned char *sl, int C, int gpc, int w, int gi,
-                                          const int8_t *digq, const float *fxq, float (&res)[4]) {
+struct StepDigits {
+    uint2 bf[2][Q<FMT>::kJ];
+    float2 fx[2];
+};
+
+template <int FMT>
+__device__ __forceinline__ void load_step_digits(const unsigned char *rec0, bool has0, bool has1,
+                                                 StepDigits<FMT> &d) {
     constexpr int WSB = Q<FMT>::kWsb;
-    constexpr int J = Q<FMT>::kJ;
     const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
-    const uint4 wa = lds128(sl + gq * C + w * 64 + t * 16);
-    const uint4 wb = lds128(sl + (gq + 8) * C + w * 64 + t * 16);
-    const uint32_t qa[4] = {wa.x, wa.y, wa.z, wa.w}, qb[4] = {wb.x, wb.y, wb.z, wb.w};
-    uint32_t ag[8], a8[8];
-    if (FMT == 0) {
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            ag[2 * j] = (qa[j] << 4) & 0xF0F0F0F0u;
-            ag[2 * j + 1] = qa[j] & 0xF0F0F0F0u;
-            a8[2 * j] = (qb[j] << 4) & 0xF0F0F0F0u;
-            a8[2 * j + 1] = qb[j] & 0xF0F0F0F0u;
-        }
-    } else {
+    for (int h = 0; h < 2; h++) {
+        const unsigned char *rec = rec0 + h * Rec<FMT>::kBytes;
+        const bool on = h == 0 ? has0 : has1;
+        const int8_t *cell = reinterpret_cast<const int8_t *>(rec) + gq * WSB + t * 8;
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            ag[j] = qa[j];
-            a8[j] = qb[j];
-        }
+        for (int j = 0; j < Q<FMT>::kJ; j++)
+            d.bf[h][j] = (gq < 3 && on) ? lds64(cell + j * 32) : make_uint2(0u, 0u);
+        d.fx[h] = on ? *reinterpret_cast<const float2 *>(
+                           reinterpret_cast<const float *>(rec + Rec<FMT>::kDigits) + 2 * t)
+                     : make_float2(0.f, 0.f);
     }
-    // One accumulator per k32 MMA, so the MMAs do not wait for each other;
-    // the integer sums are then added exactly.
-    const int8_t *cell = digq + gq * WSB + t * 8;
-    uint2 bf[J];
-#pragma unroll
-    for (int j = 0; j < J; j++) bf[j] = gq < 3 ? lds64(cell + j * 32) : make_uint2(0u, 0u);
-    int accj[J][4];
-#pragma unroll
-    for (int j = 0; j < J; j++) {
-        accj[j][0] = accj[j][1] = accj[j][2] = accj[j][3] = 0;
-        mma_s8(accj[j], ag[2 * j], a8[2 * j], ag[2 * j + 1], a8[2 * j + 1], bf[j].x, bf[j].y);
-    }
-    int acc[4];
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-        acc[i] = accj[0][i];
-#pragma unroll
-        for (int j = 1; j < J; j++) acc[i] += accj[j][i];
-    }
-    const float *sc = reinterpret_cast<const float *>(sl + kSlotCode);
-    const float s0 = sc[gq * gpc + gi], s1 = sc[(gq + 8) * gpc + gi];
-    const float2 f = *reinterpret_cast<const float2 *>(fxq + 2 * t);
-    res[0] = fmaf(i2f_exact(acc[0]), s0 * f.x, res[0]);
-    res[1] = fmaf(i2f_exact(acc[1]), s0 * f.y, res[1]);
-    res[2] = fmaf(i2f_exact(acc[2]), s1 * f.x, res[2]);
-    res[3] = fmaf(i2f_exact(acc[3]), s1 * f.y, res[3]);
 }
 
-// The warp's two warp-steps of a landed chunk together: every shared load
-// and MMA of both issued before the first result is needed (the chains of
-// one warp-step are latency-bound; two interleaved keep the tensor pipe and
-// the load unit busier). has1: the second warp-step exists.
-template <int FMT>
-__device__ __forceinline__ void gemv_pair(const unsigned char *sl, int C, int gpc, int w0, int gi0,
-                                          int gi1, bool has1, const unsigned char *rec0,
-                                          const unsigned char *rec1, float (&res)[4]) {
-    constexpr int WSB = Q<FMT>::kWsb;
-    constexpr int J = Q<FMT>::kJ;
-    const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
-    const int w1 = w0 + 8;
+// One landed slot's part for this warp: the codes of its two warp-steps
+// (rows gq and gq + 8) and the four scales they need.
+struct SlotLoad {
     uint4 wa[2], wb[2];
-    wa[0] = lds128(sl + gq * C + w0 * 64 + t * 16);
-    wb[0] = lds128(sl + (gq + 8) * C + w0 * 64 + t * 16);
-    wa[1] = has1 ? lds128(sl + gq * C + w1 * 64 + t * 16) : make_uint4(0u, 0u, 0u, 0u);
-    wb[1] = has1 ? lds128(sl + (gq + 8) * C + w1 * 64 + t * 16) : make_uint4(0u, 0u, 0u, 0u);
-    uint2 bf[2][J];
-    const unsigned char *recs[2] = {rec0, rec1};
+    float s[2][2];
+};
+
+__device__ __forceinline__ void load_slot(const unsigned char *sl, int Cp, int gps, int ws0,
+                                          int gi0, int gi1, bool has1, SlotLoad &x) {
+    const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
+    const unsigned char *ra = sl + gq * Cp + ws0 * 64 + t * 16;
+    const unsigned char *rb = ra + 8 * Cp;
+    x.wa[0] = lds128(ra);
+    x.wb[0] = lds128(rb);
+    x.wa[1] = has1 ? lds128(ra + 64) : make_uint4(0u, 0u, 0u, 0u);
+    x.wb[1] = has1 ? lds128(rb + 64) : make_uint4(0u, 0u, 0u, 0u);
+    const float *sc = reinterpret_cast<const float *>(sl + kSlotCode);
+    x.s[0][0] = sc[gq * gps + gi0];
+    x.s[0][1] = sc[(gq + 8) * gps + gi0];
+    x.s[1][0] = has1 ? sc[gq * gps + gi1] : 0.f;
+    x.s[1][1] = has1 ? sc[(gq + 8) * gps + gi1] : 0.f;
+}
+
+// The s8 tensor-core products of a slot's two warp-steps with the digits
+// (integer sums, exact).
+template <int FMT>
+__device__ __forceinline__ void mma_slot(const SlotLoad &x, const StepDigits<FMT> &d,
+                                         int (&acc)[2][4]) {
+    constexpr int J = Q<FMT>::kJ;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const int8_t *cell = reinterpret_cast<const int8_t *>(recs[h]) + gq * WSB + t * 8;
-#pragma unroll
-        for (int j = 0; j < J; j++)
-            bf[h][j] = (gq < 3 && (h == 0 || has1)) ? lds64(cell + j * 32) : make_uint2(0u, 0u);
-    }
-    int accj[2][J][4];
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint32_t qa[4] = {wa[h].x, wa[h].y, wa[h].z, wa[h].w};
-        const uint32_t qb[4] = {wb[h].x, wb[h].y, wb[h].z, wb[h].w};
+        const uint32_t qa[4] = {x.wa[h].x, x.wa[h].y, x.wa[h].z, x.wa[h].w};
+        const uint32_t qb[4] = {x.wb[h].x, x.wb[h].y, x.wb[h].z, x.wb[h].w};
         uint32_t ag[8], a8[8];
         if (FMT == 0) {
 #pragma unroll
@@ -740,32 +758,37 @@ __device__ __forceinline__ void gemv_pair(const unsigned char *sl, int C, int gp
                 a8[j] = qb[j];
             }
         }
+        // One accumulator chain per warp-step (the two warp-steps of each of
+        // the two slots in flight give four independent chains a warp).
+        int accj[J][4];
 #pragma unroll
         for (int j = 0; j < J; j++) {
-            accj[h][j][0] = accj[h][j][1] = accj[h][j][2] = accj[h][j][3] = 0;
-            mma_s8(accj[h][j], ag[2 * j], a8[2 * j], ag[2 * j + 1], a8[2 * j + 1], bf[h][j].x,
-                   bf[h][j].y);
+            accj[j][0] = accj[j][1] = accj[j][2] = accj[j][3] = 0;
+            mma_s8(accj[j], ag[2 * j], a8[2 * j], ag[2 * j + 1], a8[2 * j + 1], d.bf[h][j].x,
+                   d.bf[h][j].y);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            acc[h][i] = accj[0][i];
+#pragma unroll
+            for (int j = 1; j < J; j++) acc[h][i] += accj[j][i];
         }
     }
-    const float *sc = reinterpret_cast<const float *>(sl + kSlotCode);
+}
+
+// The integer block sums of a slot scaled (scale * digit factor) into the
+// tile's row sums.
+template <int FMT>
+__device__ __forceinline__ void scale_slot(const SlotLoad &x, const int (&acc)[2][4],
+                                           const StepDigits<FMT> &d, bool has1, float (&res)[4]) {
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         if (h == 1 && !has1) break;
-        int acc[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            acc[i] = accj[h][0][i];
-#pragma unroll
-            for (int j = 1; j < J; j++) acc[i] += accj[h][j][i];
-        }
-        const int gi = h ? gi1 : gi0;
-        const float s0 = sc[gq * gpc + gi], s1 = sc[(gq + 8) * gpc + gi];
-        const float2 f = *reinterpret_cast<const float2 *>(
-            reinterpret_cast<const float *>(recs[h] + Rec<FMT>::kDigits) + 2 * t);
-        res[0] = fmaf(i2f_exact(acc[0]), s0 * f.x, res[0]);
-        res[1] = fmaf(i2f_exact(acc[1]), s0 * f.y, res[1]);
-        res[2] = fmaf(i2f_exact(acc[2]), s1 * f.x, res[2]);
-        res[3] = fmaf(i2f_exact(acc[3]), s1 * f.y, res[3]);
+        const float2 f = d.fx[h];
+        res[0] = fmaf(i2f_exact(acc[h][0]), x.s[h][0] * f.x, res[0]);
+        res[1] = fmaf(i2f_exact(acc[h][1]), x.s[h][0] * f.y, res[1]);
+        res[2] = fmaf(i2f_exact(acc[h][2]), x.s[h][1] * f.x, res[2]);
+        res[3] = fmaf(i2f_exact(acc[h][3]), x.s[h][1] * f.y, res[3]);
     }
 }
 
@@ -778,45 +801,60 @@ __device__ __forceinline__ void gemv_tiles(const DlArgs &p, const Smem &sm, cons
     const int t0 = (int)((long long)c * g.tiles / p.W);
     const int t1 = (int)((long long)(c + 1) * g.tiles / p.W);
     const unsigned char *digv = reinterpret_cast<const unsigned char *>(sm.dig);
-    const int w0 = warp, w1 = warp + 8;  // the warp's two warp-steps of a chunk
-    const int gi0 = w0 * Q<FMT>::kStep / p.group, gi1 = w1 * Q<FMT>::kStep / p.group;
+    const int ws0 = 2 * warp;  // the warp's warp-steps of a chunk: ws0, ws0 + 1
+    const int gi0 = ws0 * Q<FMT>::kStep / p.group, gi1 = (ws0 + 1) * Q<FMT>::kStep / p.group;
     uint32_t *const err = p.err;
-    const int nch = g.nch, wact = g.wact, C = g.C, gpc = g.gpc;
-    for (int tt = t0; tt < t1; tt++) {
-        const int bt = (tt - t0) % kRedTiles;
-        float res[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int ch = 0; ch < nch; ch++, seq++) {
-            if (!wait_full(err, sm, seq)) continue;
-            const unsigned char *sl = sm.ring + (seq % kSlots) * kSlotBytes;
-            if (w0 < wact) {
-                const unsigned char *rec0 = digv + (ch * wact + w0) * Rec<FMT>::kBytes;
-                gemv_pair<FMT>(sl, C, gpc, w0, gi0, gi1, w1 < wact, rec0,
-                               rec0 + 8 * Rec<FMT>::kBytes, res);
+    const int nch = g.nch, wact = g.wact, Cp = g.Cp, gps = g.gps;
+    const bool has0 = ws0 < wact, has1 = ws0 + 1 < wact;
+    static_assert(kRedTiles % 2 == 0, "slot pairs");
+    for (int tg = t0; tg < t1; tg += kRedTiles) {
+        const int nb = min(kRedTiles, t1 - tg);
+        float res[kRedTiles][4];
+#pragma unroll
+        for (int b = 0; b < kRedTiles; b++) res[b][0] = res[b][1] = res[b][2] = res[b][3] = 0.f;
+        for (int ch = 0; ch < nch; ch++) {
+            StepDigits<FMT> d;
+            load_step_digits<FMT>(digv + (ch * wact + ws0) * Rec<FMT>::kBytes, has0, has1, d);
+#pragma unroll
+            for (int b = 0; b < kRedTiles; b++) {
+                if (b < nb) {
+                    if (wait_full(err, sm, seq)) {
+                        if (has0) {
+                            SlotLoad x;
+                            load_slot(sm.ring + (seq % kSlots) * kSlotBytes, Cp, gps, ws0, gi0,
+                                      gi1, has1, x);
+                            int a[2][4];
+                            mma_slot<FMT>(x, d, a);
+                            scale_slot<FMT>(x, a, d, has1, res[b]);
+                        }
+                        release(sm, seq);
+                    }
+                    seq++;
+                }
             }
-            release(sm, seq);
         }
         // Row sums of this warp: digit columns 0, 1 (lane quad t = 0) and 2
-        // (t = 1) of activation row 0.
-        const float ca = __shfl_down_sync(0xffffffffu, res[0], 1);
-        const float cb = __shfl_down_sync(0xffffffffu, res[2], 1);
-        if (t == 0) {
-            sm.red[(bt * kCons + warp) * 16 + gq] = (res[0] + res[1]) + ca;
-            sm.red[(bt * kCons + warp) * 16 + gq + 8] = (res[2] + res[3]) + cb;
-        }
-        if (bt == kRedTiles - 1 || tt == t1 - 1) {
-            cons_sync();
-            const int first = tt - bt;
-            if ((int)threadIdx.x < (bt + 1) * 16) {
-                const int b = threadIdx.x >> 4, r = threadIdx.x & 15;
-                float v = 0.f;
+        // (t = 1) of activation row 0; then the warps' sums in warp order.
 #pragma unroll
-                for (int w = 0; w < kCons; w++) v += sm.red[(b * kCons + w) * 16 + r];
-                int row;
-                const int m = tile_mat(g, first + b, &row);
-                if (!*sm.abort) stage_out(g, m)[row + r] = v;
+        for (int b = 0; b < kRedTiles; b++) {
+            const float ca = __shfl_down_sync(0xffffffffu, res[b][0], 1);
+            const float cb = __shfl_down_sync(0xffffffffu, res[b][2], 1);
+            if (t == 0 && b < nb) {
+                sm.red[(b * kCons + warp) * 16 + gq] = (res[b][0] + res[b][1]) + ca;
+                sm.red[(b * kCons + warp) * 16 + gq + 8] = (res[b][2] + res[b][3]) + cb;
             }
-            cons_sync();
         }
+        cons_sync();
+        if ((int)threadIdx.x < nb * 16) {
+            const int b = threadIdx.x >> 4, r = threadIdx.x & 15;
+            float v = 0.f;
+#pragma unroll
+            for (int w = 0; w < kCons; w++) v += sm.red[(b * kCons + w) * 16 + r];
+            int row;
+            const int m = tile_mat(g, tg + b, &row);
+            if (!*sm.abort) stage_out(g, m)[row + r] = v;
+        }
+        cons_sync();
     }
 }
 
@@ -1340,76 +1378,77 @@ __device__ void scribe_program(const DlArgs &p, const Smem &sm) {
     put_smem(last, kDlXn, sm.resid, p.H);
 }
 
-// A worker's program: the layer stages, each ended by an arrival.
+// A worker's program: the layer stages, each ended by an arrival. The four
+// GEMV stages share one code path (one copy of the GEMV loop and of the
+// input digitization: the instruction cache holds the whole layer).
 template <int FMT, int G>
 __device__ void worker_program(const DlArgs &p, const Smem &sm) {
     const unsigned W = (unsigned)p.W;
     const unsigned *sc = p.sync + kSyncScribe;
     const int QD = p.Hq * kD;
     unsigned seq = 0, fetches = 0;
-    int s0, s1;
     load_smem(sm.resid, p.x0, p.H);
     cons_sync();
     for (int l = 0; l < p.L; l++) {
         const DlLayer &ly = p.layers[l];
         unsigned *ctr = p.sync + kSyncStages + kCtrs * l;
         const unsigned g0 = 4u * (unsigned)l;
-        // ---- QKV: x = x1 + f, h = rmsnorm(x) digitized; q, k, v.
-        if (l > 0) {
-            dep_wait(p, sm, ctr - kCtrs + cDOWN, W);
-            resid_add(p, sm, p.F);
-        }
-        {
-            const float inv1 = resid_inv_rms(p, sm, ly.eps1);
-            my_steps<FMT>(p, p.H, &s0, &s1);
-            digitize_steps<FMT, kInNorm>(sm, s0, s1, nullptr, nullptr, ly.wn1, inv1, p.digA);
-            arrive(ctr + cDQ);
-            dep_wait(p, sm, ctr + cDQ, W, l == 0 ? nullptr : sc, g0 - 2);
-            fetch_digits<FMT>(p, sm, p.digA, p.H, fetches);
-            const StageGeo g = stage_geo<FMT>(p, kQKV);
+        for (int st = kQKV; st <= kDOWN; st++) {
+            if (st == kATTN) {
+                // ATTN (the merging CTAs also digitize the output rows).
+                dep_wait(p, sm, ctr + cQKV, W, l == 0 ? nullptr : sc, g0 - 1);
+                const AttnPlan ap = attn_plan(p, ly);
+                if ((int)blockIdx.x < p.Hkv * ap.nchunk) attention_item<FMT, G>(p, sm, ly, ap, seq);
+                arrive(ctr + cATTN);
+                continue;
+            }
+            // The stage input as a digit vector in global memory.
+            const unsigned char *dsrc;
+            int K;
+            if (st == kO) {
+                dep_wait(p, sm, ctr + cATTN, W, l == 0 ? nullptr : sc, g0);
+                dsrc = p.digO;
+                K = QD;
+            } else {
+                // QKV: x = x1 + f, h = rmsnorm(x); GU: x1 = x + o, h2 =
+                // rmsnorm(x1); DOWN: silu(gate) * up. Each worker digitizes
+                // its share of the warp-steps, then waits for the others.
+                if (st == kQKV) {
+                    if (l > 0) {
+                        dep_wait(p, sm, ctr - kCtrs + cDOWN, W);
+                        resid_add(p, sm, p.F);
+                    }
+                } else if (st == kGU) {
+                    dep_wait(p, sm, ctr + cO, W);
+                    resid_add(p, sm, p.O);
+                } else {
+                    dep_wait(p, sm, ctr + cGU, W);
+                }
+                const bool down = st == kDOWN;
+                K = down ? p.I : p.H;
+                unsigned char *dst = down ? p.digD : p.digA;
+                int s0, s1;
+                my_steps<FMT>(p, K, &s0, &s1);
+                if (down) {
+                    digitize_steps<FMT, kInSwiglu>(sm, s0, s1, p.Gb, p.Ub, nullptr, 0.f, dst);
+                } else {
+                    const float inv = resid_inv_rms(p, sm, st == kQKV ? ly.eps1 : ly.eps2);
+                    digitize_steps<FMT, kInNorm>(sm, s0, s1, nullptr, nullptr,
+                                                 st == kQKV ? ly.wn1 : ly.wn2, inv, dst);
+                }
+                const int cd = st == kQKV ? cDQ : (st == kGU ? cDGU : cDD);
+                arrive(ctr + cd);
+                // QKV overwrites q k v (scribe phase ATTN(l - 1) read them);
+                // DOWN overwrites f (S1(l) read the previous layer's).
+                const unsigned *gate = st == kQKV ? (l == 0 ? nullptr : sc) : (down ? sc : nullptr);
+                const unsigned gt = st == kQKV ? g0 - 2 : g0 + 1;
+                dep_wait(p, sm, ctr + cd, W, gate, gt);
+                dsrc = dst;
+            }
+            fetch_digits<FMT>(p, sm, dsrc, K, fetches);
+            const StageGeo g = stage_geo<FMT>(p, st);
             gemv_tiles<FMT>(p, sm, g, seq);
-            arrive(ctr + cQKV);
-        }
-        // ---- ATTN (the merging CTAs also digitize the output rows).
-        dep_wait(p, sm, ctr + cQKV, W, l == 0 ? nullptr : sc, g0 - 1);
-        {
-            const AttnPlan ap = attn_plan(p, ly);
-            if ((int)blockIdx.x < p.Hkv * ap.nchunk) attention_item<FMT, G>(p, sm, ly, ap, seq);
-            arrive(ctr + cATTN);
-        }
-        // ---- O.
-        dep_wait(p, sm, ctr + cATTN, W, l == 0 ? nullptr : sc, g0);
-        {
-            fetch_digits<FMT>(p, sm, p.digO, QD, fetches);
-            const StageGeo g = stage_geo<FMT>(p, kO);
-            gemv_tiles<FMT>(p, sm, g, seq);
-            arrive(ctr + cO);
-        }
-        // ---- GU: x1 = x + o, h2 = rmsnorm(x1) digitized; gate, up.
-        dep_wait(p, sm, ctr + cO, W);
-        resid_add(p, sm, p.O);
-        {
-            const float inv2 = resid_inv_rms(p, sm, ly.eps2);
-            my_steps<FMT>(p, p.H, &s0, &s1);
-            digitize_steps<FMT, kInNorm>(sm, s0, s1, nullptr, nullptr, ly.wn2, inv2, p.digA);
-            arrive(ctr + cDGU);
-            dep_wait(p, sm, ctr + cDGU, W);
-            fetch_digits<FMT>(p, sm, p.digA, p.H, fetches);
-            const StageGeo g = stage_geo<FMT>(p, kGU);
-            gemv_tiles<FMT>(p, sm, g, seq);
-            arrive(ctr + cGU);
-        }
-        // ---- DOWN: silu(gate) * up digitized; down.
-        dep_wait(p, sm, ctr + cGU, W);
-        {
-            my_steps<FMT>(p, p.I, &s0, &s1);
-            digitize_steps<FMT, kInSwiglu>(sm, s0, s1, p.Gb, p.Ub, nullptr, 0.f, p.digD);
-            arrive(ctr + cDD);
-            dep_wait(p, sm, ctr + cDD, W, sc, g0 + 1);
-            fetch_digits<FMT>(p, sm, p.digD, p.I, fetches);
-            const StageGeo g = stage_geo<FMT>(p, kDOWN);
-            gemv_tiles<FMT>(p, sm, g, seq);
-            arrive(ctr + cDOWN);
+            arrive(ctr + (st == kQKV ? cQKV : st == kO ? cO : st == kGU ? cGU : cDOWN));
         }
     }
     // A copy still in flight after giving up lands before the CTA exits
@@ -1446,8 +1485,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
         sm.trig[kD / 2 + threadIdx.x] = (float)cs;
     }
     __syncthreads();
-    if (warp == kCons) {
-        if (lane == 0 && (int)blockIdx.x < p.W) {
+    if (warp >= kCons) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProdRegs));
+        if (warp == kCons && lane == 0 && (int)blockIdx.x < p.W) {
             for (int l = 0; l < p.L && l < 2; l++)
                 for (int m = 0; m < 7; m++) {
                     prefetch_tensormap(p.maps + p.layers[l].map[m]);
@@ -1455,10 +1495,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
                 }
             producer<FMT>(p, sm);
         }
-    } else if ((int)blockIdx.x == p.W) {
-        scribe_program(p, sm);
     } else {
-        worker_program<FMT, G>(p, sm);
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsRegs));
+        if ((int)blockIdx.x == p.W)
+            scribe_program(p, sm);
+        else
+            worker_program<FMT, G>(p, sm);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -1628,10 +1670,14 @@ bool decode_layers_image(const DlRun &r, void *host_image, size_t bytes, const v
             const int C = rowb < kChunk ? rowb : kChunk;
             const int gpc = C * (r.format == 0 ? 2 : 1) / (int)r.group;
             const int idx = (int)(l * 14 + 2 * m);
-            if (!encode_tensor_map_2d(&maps[idx], CU_TENSOR_MAP_DATA_TYPE_UINT32, w.codes,
-                                      (uint64_t)rowb / 4, w.n, (uint64_t)rowb, (uint32_t)C / 4, 16) ||
+            // Boxes of the slot row strides (codes in 8-byte units: a padded
+            // row of 1088 bytes is 136 elements, within the 256 a box allows).
+            const int Cp = slot_code_stride(rowb, C), gps = slot_scale_stride(rowb, C, gpc);
+            if (!encode_tensor_map_2d(&maps[idx], CU_TENSOR_MAP_DATA_TYPE_UINT64, w.codes,
+                                      (uint64_t)rowb / 8, w.n, (uint64_t)rowb, (uint32_t)Cp / 8,
+                                      16) ||
                 !encode_tensor_map_2d(&maps[idx + 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales,
-                                      w.groups, w.n, w.groups * 4, (uint32_t)gpc, 16))
+                                      w.groups, w.n, w.groups * 4, (uint32_t)gps, 16))
                 return false;
             d.map[m] = idx;
         }
