@@ -201,6 +201,21 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *a) {
     return v;
 }
 
+// *a += v at GPU scope with release semantics: the writes this CTA made
+// before (ordered to this thread by a CTA barrier) are visible to a thread
+// that acquires the new value.
+__device__ __forceinline__ void red_release_add(unsigned *a, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+
+// Ticket: the old value of *a, incremented with acquire-release semantics
+// at GPU scope (the last taker sees every earlier taker's writes).
+__device__ __forceinline__ unsigned atom_acq_rel_add(unsigned *a, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(a), "r"(v) : "memory");
+    return old;
+}
+
 // L2 policy for data every CTA reads (the digit vectors).
 __device__ __forceinline__ uint64_t policy_evict_last() {
     uint64_t pol;
@@ -264,7 +279,7 @@ __device__ __forceinline__ bool poll_ge(const DlArgs &p, const Smem &sm, const u
             *sm.abort = 1;
             return false;
         }
-        __nanosleep(32);
+        if (it > 64) __nanosleep(32);
     }
 }
 
@@ -282,8 +297,7 @@ __device__ __forceinline__ void dep_wait(const DlArgs &p, const Smem &sm, const 
 __device__ __forceinline__ void arrive(unsigned *ctr) {
     cons_sync();
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(ctr, 1u);
+        red_release_add(ctr, 1u);
     }
 }
 
@@ -591,7 +605,7 @@ __device__ __forceinline__ void digits_step(float (&v)[Q<FMT>::kStep / 32], int8
     }
 }
 
-enum StageIn { kInNorm = 0, kInVec = 1, kInSwiglu = 2 };
+enum StageIn { kInNorm = 0, kInVec = 1, kInSwiglu = 2, kInShared = 3 };
 
 // A stage input is digitized once per stage (warp-steps spread over the
 // workers) into a digit vector in global memory, one record per warp-step:
@@ -604,31 +618,61 @@ struct Rec {
 };
 
 // Warp-steps [s0, s1) of a stage input, one per warp: rmsnorm(resid) * w
-// (norm.rs arithmetic: two rounded multiplies), a private vector, or
-// silu(a) * b (the elementwise silu_mul expression).
+// (norm.rs arithmetic: two rounded multiplies), a private vector (global,
+// or shared memory holding the steps from s0 on), or silu(a) * b (the
+// elementwise silu_mul expression).
 template <int FMT, int MODE>
 __device__ __forceinline__ void digitize_steps(const Smem &sm, int s0, int s1, const float *src,
                                                const float *src2, const float *wn, float inv,
                                                unsigned char *out) {
     constexpr int PER = Q<FMT>::kStep / 32;
+    constexpr int kBatch = 4;  // steps of a warp whose loads are in flight together
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int st = s0 + warp; st < s1; st += kCons) {
-        const int k = st * Q<FMT>::kStep + lane * PER;
-        float v[PER];
+    for (int base = s0 + warp; base < s1; base += kCons * kBatch) {
+        float x[kBatch][PER], y[kBatch][PER];
 #pragma unroll
-        for (int i = 0; i < PER; i++) {
-            if (MODE == kInNorm) {
-                v[i] = __fmul_rn(__fmul_rn(sm.resid[k + i], inv), __ldg(wn + k + i));
-            } else if (MODE == kInVec) {
-                v[i] = __ldcg(src + k + i);
-            } else {
-                const float a = __ldcg(src + k + i), b = __ldcg(src2 + k + i);
-                v[i] = __fmul_rn(__fmul_rn(a, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)))), b);
+        for (int q = 0; q < kBatch; q++) {
+            const int st = base + q * kCons;
+            const int k = st * Q<FMT>::kStep + lane * PER;
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                x[q][i] = 0.f, y[q][i] = 0.f;
+                if (st < s1) {
+                    if (MODE == kInNorm) {
+                        x[q][i] = sm.resid[k + i];
+                        y[q][i] = __ldg(wn + k + i);
+                    } else if (MODE == kInVec) {
+                        x[q][i] = __ldcg(src + k + i);
+                    } else if (MODE == kInShared) {  // src holds the steps from s0 on
+                        x[q][i] = src[k - s0 * Q<FMT>::kStep + i];
+                    } else {
+                        x[q][i] = __ldcg(src + k + i);
+                        y[q][i] = __ldcg(src2 + k + i);
+                    }
+                }
             }
         }
-        unsigned char *rec = out + (size_t)st * Rec<FMT>::kBytes;
-        digits_step<FMT>(v, reinterpret_cast<int8_t *>(rec),
-                         reinterpret_cast<float *>(rec + Rec<FMT>::kDigits));
+#pragma unroll
+        for (int q = 0; q < kBatch; q++) {
+            const int st = base + q * kCons;
+            if (st >= s1) break;
+            float v[PER];
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                if (MODE == kInNorm) {
+                    v[i] = __fmul_rn(__fmul_rn(x[q][i], inv), y[q][i]);
+                } else if (MODE == kInSwiglu) {
+                    const float a = x[q][i];
+                    v[i] = __fmul_rn(__fmul_rn(a, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-a)))),
+                                     y[q][i]);
+                } else {
+                    v[i] = x[q][i];
+                }
+            }
+            unsigned char *rec = out + (size_t)st * Rec<FMT>::kBytes;
+            digits_step<FMT>(v, reinterpret_cast<int8_t *>(rec),
+                             reinterpret_cast<float *>(rec + Rec<FMT>::kDigits));
+        }
     }
 }
 
@@ -664,6 +708,10 @@ template <int FMT>
 __device__ __forceinline__ void fetch_digits(const DlArgs &p, const Smem &sm,
                                              const unsigned char *src, int K, unsigned &fetches) {
     const uint32_t bytes = (uint32_t)(K / Q<FMT>::kStep * Rec<FMT>::kBytes);
+    // The destination was last written by ordinary stores (the attention
+    // scratch aliases it): order them before the copy.
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    cons_sync();
     if (threadIdx.x == 0 && !*sm.abort) {
         asm volatile("fence.proxy.async.global;" ::: "memory");
         mbar_arrive_expect_tx(sm.dbar, bytes);
@@ -963,8 +1011,7 @@ __device__ void resid_add_smem(const DlArgs &p, const Smem &sm, const float *v) 
 // the barrier that follows its loads): workers may overwrite them.
 __device__ __forceinline__ void scribe_signal(const DlArgs &p) {
     if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(p.sync + kSyncScribe, 1u);
+        red_release_add(p.sync + kSyncScribe, 1u);
     }
 }
 
@@ -999,17 +1046,36 @@ struct AttnScratch {
     static constexpr int kMl = kMo + kCons * G * kD;  // [kCons][G][2] warp max / sum
     static constexpr int kW = kMl + kCons * G * 2;  // [G][kCons] warp weights
     static constexpr int kRmax = kW + G * kCons;    // [G] row maxima
-    static constexpr int kEnd = kRmax + G;          // then the chunk merge: [G][nchunk] x 2 + [G]
+    static constexpr int kOut = (kRmax + G + 3) / 4 * 4;  // [G][D] this kv head's output rows
+    // The chunk merge splits the chunks of every output float4 over kParts
+    // threads (all consumer threads busy): [kParts][G][D] partial sums.
+    static constexpr int kParts = kConsThreads / (32 * G);
+    static constexpr int kPart = kOut + G * kD;
+    static constexpr int kEnd = kPart + kParts * G * kD;  // then [G][nchunk] x 2 + [G]
 };
 
-// The G attention-output rows of kv head kvh, written to ATT by this CTA,
-// as digit records of the o projection's input.
+// Floats of the attention scratch for GQA group G and at most cap chunks
+// per kv head (host and device agree).
+__host__ __device__ inline int attn_scratch_floats(int G, int cap) {
+    int end = 0;
+    switch (G) {
+        case 1: end = AttnScratch<1>::kEnd; break;
+        case 2: end = AttnScratch<2>::kEnd; break;
+        case 4: end = AttnScratch<4>::kEnd; break;
+        default: end = AttnScratch<8>::kEnd; break;
+    }
+    return end + 2 * G * cap + G;
+}
+
+// The G attention-output rows of kv head kvh (in the scratch), as digit
+// records of the o projection's input.
 template <int FMT, int G>
 __device__ __forceinline__ void digitize_heads(const DlArgs &p, const Smem &sm, int kvh) {
-    cons_sync();  // the rows are in ATT
+    cons_sync();  // the rows are in the scratch
     constexpr int kSteps = G * kD / Q<FMT>::kStep;
     const int s0 = kvh * kSteps;
-    digitize_steps<FMT, kInVec>(sm, s0, s0 + kSteps, p.ATT, nullptr, nullptr, 0.f, p.digO);
+    const float *rows = reinterpret_cast<const float *>(sm.dig) + AttnScratch<G>::kOut;
+    digitize_steps<FMT, kInShared>(sm, s0, s0 + kSteps, rows, nullptr, nullptr, 0.f, p.digO);
 }
 
 template <int FMT, int G>
@@ -1090,7 +1156,7 @@ __device__ __forceinline__ void attention_item(const DlArgs &p, const Smem &sm, 
     // half of the values a lane carries to its partner), after which lane
     // l holds the score of pair l / REP (row r = pair / KPW, key i = pair %
     // KPW).
-    constexpr int KPW = (32 / G) < 4 ? (32 / G) : 4;
+    constexpr int KPW = (32 / G) < 8 ? (32 / G) : 8;
     constexpr int RS = KPW / 2;
     constexpr int NV = G * KPW, REP = 32 / NV;
     constexpr int LOG = NV == 32 ? 5 : NV == 16 ? 4 : NV == 8 ? 3 : 2;
@@ -1223,7 +1289,9 @@ __device__ __forceinline__ void attention_item(const DlArgs &p, const Smem &sm, 
         const long long row = (long long)kvh * G + r;
         if (!*sm.abort) {
             if (ap.nchunk == 1) {
-                p.ATT[row * kD + d] = __fdiv_rn(acc, ll);
+                const float out = __fdiv_rn(acc, ll);
+                p.ATT[row * kD + d] = out;
+                scr[S::kOut + r * kD + d] = out;
             } else {
                 p.part_o[(row * ap.nchunk + chunk) * kD + d] = acc;
                 if (d == 0) {
@@ -1241,10 +1309,8 @@ __device__ __forceinline__ void attention_item(const DlArgs &p, const Smem &sm, 
     // The last CTA of this kv head merges the chunks in ascending order.
     cons_sync();
     if (tid == 0) {
-        __threadfence();
-        const unsigned ticket = atomicAdd(p.sync + kSyncTickets + kvh, 1u);
+        const unsigned ticket = atom_acq_rel_add(p.sync + kSyncTickets + kvh, 1u);
         *sm.flag = ticket == (unsigned)(ap.nchunk - 1);
-        __threadfence();
     }
     cons_sync();
     if (!*sm.flag) return;
@@ -1252,46 +1318,86 @@ __device__ __forceinline__ void attention_item(const DlArgs &p, const Smem &sm, 
     float *lt = wt + G * ap.nchunk;   // [G][nchunk] chunk denominators
     float *inv = lt + G * ap.nchunk;  // [G]
     const long long row0 = (long long)kvh * G;
+    // Every output float4 of the G rows: its chunks split over kParts
+    // threads (ascending ranges), the parts then added in ascending order.
+    // The first batch of this thread's partials is loaded together with the
+    // chunk maxima / sums, before the chunk weights are known.
+    constexpr int kItems = G * kD / 4, kParts = S::kParts, kBatch = 16;
+    static_assert(kItems * kParts == kConsThreads, "merge threads");
+    const int mi = tid % kItems, part = tid / kItems;
+    const int r = mi / (kD / 4), d4 = mi - r * (kD / 4);
+    const int c0 = part * ap.nchunk / kParts, c1 = (part + 1) * ap.nchunk / kParts;
+    const float4 *src =
+        reinterpret_cast<const float4 *>(p.part_o + (row0 + r) * ap.nchunk * kD) + d4;
+    float4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; j++)
+        v[j] = c0 + j < c1 ? __ldcg(src + (size_t)(c0 + j) * (kD / 4))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int i = tid; i < G * ap.nchunk; i += kConsThreads) {
-        const int r = i / ap.nchunk, cc = i - r * ap.nchunk;
-        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.part_ml) + (row0 + r) * ap.nchunk + cc);
+        const int rr = i / ap.nchunk, cc = i - rr * ap.nchunk;
+        const float2 ml = __ldcg(reinterpret_cast<const float2 *>(p.part_ml) + (row0 + rr) * ap.nchunk + cc);
         wt[i] = ml.x;
         lt[i] = ml.y;
     }
     cons_sync();
     if (warp < G) {
-        const int r = warp;
+        const int rr = warp;
         float mm = -INFINITY;
-        for (int cc = lane; cc < ap.nchunk; cc += 32) mm = fmaxf(mm, wt[r * ap.nchunk + cc]);
+        for (int cc = lane; cc < ap.nchunk; cc += 32) mm = fmaxf(mm, wt[rr * ap.nchunk + cc]);
         mm = warp_max(mm);
         __syncwarp();
         for (int cc = lane; cc < ap.nchunk; cc += 32) {
-            const float mc = wt[r * ap.nchunk + cc];
-            wt[r * ap.nchunk + cc] = mc == -INFINITY ? 0.f : expf(mc - mm);
+            const float mc = wt[rr * ap.nchunk + cc];
+            wt[rr * ap.nchunk + cc] = mc == -INFINITY ? 0.f : expf(mc - mm);
         }
         __syncwarp();
         if (lane == 0) {
             float ll = 0.f;
             for (int cc = 0; cc < ap.nchunk; cc++)
-                ll = fmaf(lt[r * ap.nchunk + cc], wt[r * ap.nchunk + cc], ll);
-            inv[r] = ll;
+                ll = fmaf(lt[rr * ap.nchunk + cc], wt[rr * ap.nchunk + cc], ll);
+            inv[rr] = ll;
         }
     }
     cons_sync();
-    for (int i = tid; i < G * kD; i += kConsThreads) {
-        const int r = i / kD, d = i - r * kD;
-        const float *src = p.part_o + (row0 + r) * ap.nchunk * kD + d;
-        float acc = 0.f;
-        // Chunks in ascending order, sixteen partials in flight per batch.
-        for (int c0 = 0; c0 < ap.nchunk; c0 += 16) {
-            float v[16];
+    {
+        const float *w = wt + r * ap.nchunk;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int cb = c0; cb < c1; cb += kBatch) {
+            if (cb != c0) {
 #pragma unroll
-            for (int j = 0; j < 16; j++) v[j] = c0 + j < ap.nchunk ? __ldcg(src + (c0 + j) * kD) : 0.f;
+                for (int j = 0; j < kBatch; j++)
+                    v[j] = cb + j < c1 ? __ldcg(src + (size_t)(cb + j) * (kD / 4))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
-            for (int j = 0; j < 16; j++)
-                if (c0 + j < ap.nchunk) acc = fmaf(v[j], wt[r * ap.nchunk + c0 + j], acc);
+            for (int j = 0; j < kBatch; j++) {
+                if (cb + j < c1) {
+                    const float f = w[cb + j];
+                    acc.x = fmaf(v[j].x, f, acc.x);
+                    acc.y = fmaf(v[j].y, f, acc.y);
+                    acc.z = fmaf(v[j].z, f, acc.z);
+                    acc.w = fmaf(v[j].w, f, acc.w);
+                }
+            }
         }
-        if (!*sm.abort) p.ATT[(row0 + r) * kD + d] = __fdiv_rn(acc, inv[r]);
+        reinterpret_cast<float4 *>(scr + S::kPart)[part * kItems + mi] = acc;
+        cons_sync();
+        if (tid < kItems) {
+            const float4 *pp = reinterpret_cast<const float4 *>(scr + S::kPart);
+            float4 a = pp[tid];
+#pragma unroll
+            for (int q = 1; q < kParts; q++) {
+                const float4 b = pp[q * kItems + tid];
+                a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+            }
+            const float den = inv[r];
+            const float4 out = make_float4(__fdiv_rn(a.x, den), __fdiv_rn(a.y, den),
+                                           __fdiv_rn(a.z, den), __fdiv_rn(a.w, den));
+            if (!*sm.abort)
+                reinterpret_cast<float4 *>(p.ATT + (row0 + r) * kD)[d4] = out;
+            reinterpret_cast<float4 *>(scr + S::kOut + r * kD)[d4] = out;
+        }
     }
     if (tid == 0) p.sync[kSyncTickets + kvh] = 0u;
     digitize_heads<FMT, G>(p, sm, kvh);
@@ -1556,9 +1662,7 @@ Layout layout_for(const DlRun &r, int sms) {
     L.nchunk_cap = W / (int)r.kv_heads;
     const int G = (int)(r.heads / r.kv_heads);
     // The attention scratch (aliasing the digits) must fit as well.
-    const size_t attn_floats = (size_t)(G + 2) * kD + (size_t)kCons * G * kD +
-                               (size_t)kCons * G * 2 + (size_t)G * kCons + G +
-                               (size_t)2 * G * L.nchunk_cap + G;
+    const size_t attn_floats = (size_t)attn_scratch_floats(G, L.nchunk_cap);
     size_t dig_region = (size_t)L.dig_bytes;
     if (attn_floats * 4 > dig_region) dig_region = attn_floats * 4;
     dig_region = (dig_region + 15) / 16 * 16;
