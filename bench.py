@@ -9,18 +9,23 @@ quantized to symmetric INT4 group 128 (generated on the device), f32
 activations and KV cache, a 1024-token random prompt (prefill, untimed), then
 greedy decode. One timed step = one decode token per sequence through
 Engine::step (slc_llama_step): every command of the decode program goes
-through slc_dispatch. With N > 1 (torchrun) the model is tensor-parallel over
-N GPUs (NCCL all-reduce after o/down, all-gather of the logits); the total
+through slc_dispatch; with command capture the step replays as one CUDA
+graph, and at batch 1 on one GPU its 32 layers run as one persistent kernel
+(decode_layers_kernel). With N > 1 (torchrun) the model is tensor-parallel
+over N GPUs (all-reduce after o/down, all-gather of the logits); the total
 work is fixed, so scaling is "strong".
 
 Reported: `value` = decode tok/s from the device time of the steps (CUDA
 events on the device stream, max over ranks); `e2e` = the same through the
 public API with host buffers (ids/positions uploaded, logits downloaded every
-step, host wall clock, max over ranks); `roofline` = the INT4 decode GEMV
-(the dominant kernel) measured live on the model's own weights;
-`cpu_baseline` = the CPU oracle (the restated reference kernels) on this
-host's cores. The weights streamed per step (~4 GB) exceed the 126 MB L2, so
-no flush is needed between steps.
+step, host wall clock, max over ranks); `roofline` = the dominant kernel:
+the persistent decode-layer kernel, timed on the device every timed step
+by its own global-timer stamps at start (first CTA) and end (last CTA to
+exit) (where it does not run: the quantized
+decode GEMVs measured live on the model's own weights); `cpu_baseline` = the
+CPU oracle (the restated reference kernels) on this host's cores. The
+weights streamed per step (~4 GB) exceed the 126 MB L2, so no flush is
+needed between steps.
 """
 from __future__ import annotations
 
@@ -43,6 +48,7 @@ FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tok/s (Llama-3-8B-shaped llama-dense, INT4 g128)"
 METRIC_70B = "decode tok/s (Llama-2-70B-shaped llama-dense, INT8 g128)"
 TRAFFIC_PROFILE = os.path.join(ROOT, "profiles", "gemv_imma_int4_28672x4096_m1.md")
+FUSED_PROFILE = os.path.join(ROOT, "profiles", "decode_layers_8b_int4_4layers.md")
 
 
 def parse_args(argv=None):
@@ -88,11 +94,11 @@ def bf16_peak():
         return 1590.0, "fallback"
 
 
-def profile_traffic_ratio():
-    """DRAM bytes / algorithmic bytes of the decode GEMV, from the committed
-    ncu summary of one full-size launch (the traffic_ratio line)."""
+def profile_traffic_ratio(path=TRAFFIC_PROFILE):
+    """DRAM bytes / algorithmic bytes of a kernel, from its committed ncu
+    summary (the traffic_ratio line)."""
     try:
-        for line in open(TRAFFIC_PROFILE):
+        for line in open(path):
             if line.strip().startswith("traffic_ratio:"):
                 return float(line.split(":", 1)[1].strip().split()[0])
     except Exception:
@@ -265,6 +271,54 @@ def run_reference(args, dist: Dist):
 
 # ------------------------------------------------------------ GPU arm ------
 
+def fused_layer_bytes(cfg, past):
+    """Algorithmic HBM bytes of one layer of the persistent decode kernel at
+    one token: the seven quantized matrices (codes + one f32 scale per
+    group), the layer's cached keys and values at positions [0, past) read
+    once and the new position's written, and the two norm weights."""
+    D = cfg.head_dim
+    mats = [(cfg.heads * D, cfg.hidden), (cfg.kv_heads * D, cfg.hidden),
+            (cfg.kv_heads * D, cfg.hidden), (cfg.hidden, cfg.heads * D),
+            (cfg.inter, cfg.hidden), (cfg.inter, cfg.hidden), (cfg.hidden, cfg.inter)]
+    int4 = int(cfg.quant) == 0
+    w = sum((n * k // 2 if int4 else n * k) + 4 * n * (k // cfg.group_size) for n, k in mats)
+    kv = 2 * past * cfg.kv_heads * D * 4 + 2 * cfg.kv_heads * D * 4
+    return w + kv + 2 * cfg.hidden * 4
+
+
+def streamed_weight_bytes(cfg):
+    """Quantized weight bytes one decode step streams, per GPU (the layers'
+    matrices and the vocabulary projection, split over the TP ranks)."""
+    per_layer = fused_layer_bytes(cfg, 0) - 2 * cfg.kv_heads * cfg.head_dim * 4 - 2 * cfg.hidden * 4
+    return (cfg.layers * per_layer + model_lm_bytes(cfg)) / max(1, cfg.tp_world)
+
+
+def model_lm_bytes(cfg):
+    """Vocabulary projection (quantized) and final norm bytes of one step."""
+    int4 = int(cfg.quant) == 0
+    n, k = cfg.vocab, cfg.hidden
+    return (n * k // 2 if int4 else n * k) + 4 * n * (k // cfg.group_size) + 4 * k
+
+
+def fused_roofline(cfg, fused_ms, pasts, peak):
+    """Roofline of the persistent decode-layer kernel (one launch = every
+    layer of one decode step), timed by the kernel's own device global-timer
+    stamps (start of CTA 0, end of the last CTA to exit) in every timed step."""
+    launch_s = statistics.mean(fused_ms) / 1e3
+    per_launch = statistics.mean(cfg.layers * fused_layer_bytes(cfg, p) for p in pasts)
+    achieved = per_launch / launch_s / 1e9
+    ratio = profile_traffic_ratio(FUSED_PROFILE)
+    return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
+            "frac": achieved / peak[0],
+            "traffic": ratio * per_launch if ratio is not None else None,
+            "kernel": "decode_layers_kernel (persistent, all %d layers of a decode step)"
+                      % cfg.layers,
+            "algorithmic_bytes_per_launch": per_launch, "launch_us": launch_s * 1e6,
+            "launches_timed": len(fused_ms), "peak_source": peak[1],
+            "traffic_source": ("ncu dram bytes of a 4-layer launch per algorithmic byte, "
+                               "scaled to this launch" if ratio is not None else None)}
+
+
 def _gemv_roofline(dev, model, cfg, batch, peak):
     """Live measurement of the INT4 decode GEMV (MatMulNT, M = batch) on the
     model's own quantized weights, every layer in turn (working set ~4 GB, cold
@@ -418,7 +472,9 @@ def run_ours(args, dist: Dist):
     world, rank = dist.world, dist.rank
     torch.cuda.set_device(dist.local)
     dev = CudaDevice(dist.local)
-    # Command capture: repeated decode steps replay as one CUDA graph each.
+    # Command capture: repeated decode steps replay as one CUDA graph each
+    # (at batch 1 without tensor parallelism the layers of a step run as one
+    # persistent kernel, which stamps its own start and end on the device).
     dev.set_capture(True)
     if world > 1:
         uid = comm_unique_id() if rank == 0 else None
@@ -437,8 +493,7 @@ def run_ours(args, dist: Dist):
     synthetic_kv = args.synthetic_kv or args.model == "70b"
     if synthetic_kv:
         # The decode step's cost does not depend on the cached keys/values:
-        # fill the cache instead of running the prefill (for 70B at batch 16 x
-        # 2048 tokens the prefill is ~4.5 PFLOP on the SIMT prefill path).
+        # fill the cache instead of running the prefill (--synthetic-kv).
         from starlight_b200.device import BufferRef
         kb, kn = model.kv_buffer()
         dev.fill_normal(BufferRef(kb, 0, kn), seed=99, mean=0.0, std=1.0)
@@ -460,17 +515,27 @@ def run_ours(args, dist: Dist):
     dist.barrier()
     dev.synchronize()
     device_ms = 0.0
-    w0 = time.perf_counter()
+    fused_ms, pasts = [], []
+    wall = 0.0
     # NVTX range (a no-op without a profiler) so a launch list can select the
     # timed decode steps: ncu --nvtx --nvtx-include "decode/".
     torch.cuda.nvtx.range_push("decode")
     for _ in range(args.steps):
+        # Host clock around the public call and the greedy pick (the step
+        # returns the logits in host memory); the kernel-timing query below
+        # stays outside it.
+        w0 = time.perf_counter()
         logits = model.step(DECODE, ids, np.full(B, past, np.uint32), 1, past)
-        device_ms += model.last_step_ms()
         ids = logits.argmax(axis=1).astype(np.uint32)
+        wall += time.perf_counter() - w0
+        device_ms += model.last_step_ms()
+        if world == 1:
+            fs = dev.decode_fusion_stats()
+            if fs["last_ms"] > 0:
+                fused_ms.append(fs["last_ms"])
+                pasts.append(past)
         past += 1
     dev.synchronize()
-    wall = time.perf_counter() - w0
     torch.cuda.nvtx.range_pop()
     dist.barrier()
     launches = dev.launch_count() - launches0
@@ -481,7 +546,16 @@ def run_ours(args, dist: Dist):
     result = None
     if rank == 0:
         peak = hbm_peak()
-        roof = _gemv_roofline(dev, model, cfg, B, peak) if world == 1 else None
+        if world == 1 and len(fused_ms) == args.steps:
+            roof = fused_roofline(cfg, fused_ms, pasts, peak)
+            roof["step"] = {"achieved": (cfg.layers * statistics.mean(
+                                fused_layer_bytes(cfg, p) for p in pasts) + model_lm_bytes(cfg))
+                            / (device_ms / args.steps / 1e3) / 1e9,
+                            "note": "whole decode step: fused layers + final norm + "
+                                    "vocabulary projection bytes over the step time"}
+            roof["step"]["frac"] = roof["step"]["achieved"] / peak[0]
+        else:
+            roof = _gemv_roofline(dev, model, cfg, B, peak) if world == 1 else None
         norm = rmsnorm_gbs(dev, peak) if world == 1 else None
         value = B * args.steps / (device_ms / 1e3)
         e2e = B * args.steps / wall
@@ -498,7 +572,8 @@ def run_ours(args, dist: Dist):
                        "quant": "int4 g128" if args.model == "8b" else "int8 g128",
                        "global_batch": B, "seq_len": T,
                        "parallelism": f"tp{world}" if world > 1 else "single",
-                       "l2": "no flush: ~4 GB of weights streamed per step (> 126 MB L2)",
+                       "l2": "no flush: %.2f GB of quantized weights streamed per step per "
+                             "GPU (> 126 MB L2)" % (streamed_weight_bytes(cfg) / 1e9),
                        "commands_per_step": model.command_count(DECODE)},
             "clocks": clocks,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * 4 * B,

@@ -271,6 +271,25 @@ typedef struct {
 } slc_capture_info;
 int slc_capture_stats(const slc_device *device, slc_capture_info *out);
 
+/* ---- EXTENSION: persistent decode-layer fusion ----------------------------
+ * With capture enabled, a run of batch-1 llama-dense layers (the sixteen
+ * commands per layer of the llama-dense lowering, one token, one sequence,
+ * no tensor parallelism) executes as one cooperative kernel launch. The
+ * environment variable SLC_DECODE_FUSION=0, read when capture is enabled,
+ * keeps the per-command kernels. slc_decode_fusion_stats reports the fused
+ * launches the library enqueued (a launch captured into a graph counts once,
+ * however often the graph replays), those the runtime refused (the commands
+ * then ran unfused) and the device time of the most recent execution in
+ * milliseconds (-1 when none finished), from the kernel's own global-timer
+ * stamps of its start and end; it waits for the device stream. */
+typedef struct {
+    uint64_t launched;
+    uint64_t refused;
+    float last_ms;
+    float reserved;
+} slc_decode_fusion_info;
+int slc_decode_fusion_stats(const slc_device *device, slc_decode_fusion_info *out);
+
 /* ---- EXTENSION: tensor parallelism over NCCL -----------------------------
  * slc_comm_unique_id fills 128 bytes on one rank (an ncclUniqueId) that the
  * caller broadcasts; every rank then calls slc_comm_init with it. NCCL is

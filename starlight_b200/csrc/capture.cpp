@@ -128,6 +128,11 @@ extern "C" int slc_capture_stats(const slc_device *d, slc_capture_info *out) {
     return SLC_OK;
 }
 
+extern "C" int slc_decode_fusion_stats(const slc_device *d, slc_decode_fusion_info *out) {
+    if (!d || !out) return SLC_ERR_EXECUTION;
+    return decode_run_stats(d, out);
+}
+
 void release_capture(slc_device *d) {
     CaptureState *cs = d->capture;
     if (!cs) return;

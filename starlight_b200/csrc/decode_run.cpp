@@ -33,6 +33,7 @@
 
 #include <new>
 
+#include <string>
 #include <unordered_map>
 #include <vector>
 
@@ -311,6 +312,25 @@ void decode_run_release(slc_device *d) {
     cudaFreeHost(s->host_image);
     delete s;
     d->decode = nullptr;
+}
+
+int decode_run_stats(const slc_device *d, slc_decode_fusion_info *out) {
+    *out = slc_decode_fusion_info{};
+    out->last_ms = -1.f;
+    const DecodeRunState *s = d->decode;
+    if (!s) return SLC_OK;
+    out->launched = s->launched;
+    out->refused = s->refused;
+    // The kernel's own global-timer stamps of its latest launch (start, end).
+    unsigned long long t[2] = {0, 0};
+    cudaSetDevice(d->ordinal);
+    if (s->launched > 0 && cudaStreamSynchronize(d->stream) == cudaSuccess &&
+        cudaMemcpy(t, s->sync + slc::k::kDecodeStampWord, sizeof(t), cudaMemcpyDeviceToHost) ==
+            cudaSuccess &&
+        t[1] > t[0])
+        out->last_ms = (float)((double)(t[1] - t[0]) / 1e6);
+    cudaGetLastError();
+    return SLC_OK;
 }
 
 void decode_run_invalidate(slc_device *d) {

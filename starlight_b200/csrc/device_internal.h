@@ -138,6 +138,7 @@ int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, u
 // Persistent decode-layer fusion (decode_run.cpp), created with capture.
 int decode_run_create(slc_device *d);
 void decode_run_release(slc_device *d);
+int decode_run_stats(const slc_device *d, slc_decode_fusion_info *out);
 // Drops the program images of captured graphs (with the graphs).
 void decode_run_invalidate(slc_device *d);
 // Commands at the start of cmds[0..n) that form whole decoder layers the

@@ -129,7 +129,7 @@ enum Stage { kQKV = 0, kATTN = 1, kO = 2, kGU = 3, kDOWN = 4 };
 // Arrival counters of a layer: the three digitize phases (DQ, DGU, DD)
 // and the five stages.
 enum Ctr { cDQ = 0, cQKV, cATTN, cO, cDGU, cGU, cDD, cDOWN, kCtrs };
-static_assert(kSyncStages + kCtrs * kMaxLayers <= kDecodeSyncWords, "sync words");
+static_assert(kSyncStages + kCtrs * kMaxLayers <= kDecodeStampWord, "sync words");
 enum { kMq = 0, kMk, kMv, kMo, kMgate, kMup, kMdown };
 
 struct DlLayer {
@@ -1571,6 +1571,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
     extern __shared__ __align__(1024) unsigned char smem[];
     const Smem sm = carve(p, smem);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0 && blockIdx.x == 0)
+        reinterpret_cast<unsigned long long *>(p.sync + kDecodeStampWord)[0] = global_ns();
     if (threadIdx.x == 0) {
         for (int i = 0; i < kSlots; i++) {
             mbar_init(&sm.full[i], 1);
@@ -1615,6 +1617,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
         if (ticket == gridDim.x - 1) {  // every CTA is past its last wait
             for (int i = 0; i < kSyncStages + kCtrs * p.L; i++)
                 *reinterpret_cast<volatile unsigned *>(p.sync + i) = 0u;
+            reinterpret_cast<unsigned long long *>(p.sync + kDecodeStampWord)[1] = global_ns();
             __threadfence();
         }
     }

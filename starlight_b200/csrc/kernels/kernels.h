@@ -232,8 +232,12 @@ size_t decode_layers_scratch_bytes(const DlRun &r);
 // Writes the run's program image (TMA tensor maps of every weight and the
 // layer table) into host memory; the caller copies it to dev_image.
 bool decode_layers_image(const DlRun &r, void *host_image, size_t bytes, const void *dev_image);
-// sync: zeroed device words (kDecodeSyncWords), left zeroed by the kernel.
+// sync: zeroed device words (kDecodeSyncWords), left zeroed by the kernel
+// except the last four: the device global-timer stamps (ns) of the latest
+// launch's start (CTA 0 at entry) and end (the last CTA to exit), two u64
+// at word kDecodeStampWord.
 constexpr int kDecodeSyncWords = 2048;
+constexpr int kDecodeStampWord = kDecodeSyncWords - 4;
 cudaError_t decode_layers(cudaStream_t s, const DlRun &r, const void *dev_image, void *scratch,
                           size_t scratch_bytes, unsigned *sync, uint32_t *err);
 

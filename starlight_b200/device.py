@@ -138,6 +138,11 @@ class _CaptureInfo(C.Structure):
                 ("replayed_commands", C.c_uint64), ("eager_commands", C.c_uint64)]
 
 
+class _FusionInfo(C.Structure):
+    _fields_ = [("launched", C.c_uint64), ("refused", C.c_uint64), ("last_ms", C.c_float),
+                ("reserved", C.c_float)]
+
+
 class _Options(C.Structure):
     _fields_ = [("workspace_bytes", C.c_uint64), ("staging_bytes", C.c_uint64)]
 
@@ -279,6 +284,7 @@ def load_library():
         "slc_set_capture": (C.c_int, [P, C.c_int]),
         "slc_flush": (C.c_int, [P]),
         "slc_capture_stats": (C.c_int, [P, C.POINTER(_CaptureInfo)]),
+        "slc_decode_fusion_stats": (C.c_int, [P, C.POINTER(_FusionInfo)]),
         "slc_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
         "slc_comm_init": (C.c_int, [P, C.POINTER(C.c_uint8), C.c_int, C.c_int]),
         "slc_comm_world": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
@@ -300,7 +306,7 @@ def exported_symbols():
             "slc_dequantize", "slc_copy_f32_from_device", "slc_buffer_device_ptr", "slc_release",
             "slc_fill_normal",
             "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture", "slc_flush",
-            "slc_capture_stats",
+            "slc_capture_stats", "slc_decode_fusion_stats",
             "slc_comm_unique_id", "slc_comm_init", "slc_comm_world"]
 
 
@@ -453,6 +459,15 @@ class CudaDevice:
         info = _CaptureInfo()
         self._check(self._lib.slc_capture_stats(self._d, C.byref(info)))
         return {f: int(getattr(info, f)) for f, _ in _CaptureInfo._fields_}
+
+    def decode_fusion_stats(self) -> dict:
+        """Persistent decode-layer launches enqueued / refused and the device
+        time (ms, from the kernel's global-timer stamps) of the latest one;
+        waits for the device stream."""
+        info = _FusionInfo()
+        self._check(self._lib.slc_decode_fusion_stats(self._d, C.byref(info)))
+        return {"launched": int(info.launched), "refused": int(info.refused),
+                "last_ms": float(info.last_ms)}
 
     def comm_init(self, unique_id: bytes, rank: int, world: int):
         buf = (C.c_uint8 * 128)(*unique_id)
