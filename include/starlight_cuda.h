@@ -297,6 +297,12 @@ int slc_decode_fusion_stats(const slc_device *device, slc_decode_fusion_info *ou
 int slc_comm_unique_id(uint8_t out_id[128]);
 int slc_comm_init(slc_device *device, const uint8_t unique_id[128], int rank, int world);
 int slc_comm_world(const slc_device *device, int *rank, int *world);
+/* Whether the peer-memory paths are on (all ranks agreed at slc_comm_init):
+ * the fused all-reduce + Add + RmsNorm kernel, and persistent decode-layer
+ * fusion under tensor parallelism (exchanges inside the kernel). Off when any
+ * rank failed to map its peers or set SLC_PEER_ALLREDUCE=0 (both) or
+ * SLC_DECODE_FUSION=0 (the second); NCCL carries the all-reduces then. */
+int slc_comm_peer_status(const slc_device *device, int *peer_allreduce, int *decode_fusion);
 
 /* ---- EXTENSION (no counterpart in the reference): quantized matmul that
  * allocates nothing ---------------------------------------------------------

@@ -69,9 +69,11 @@ struct CommState {
     ncclComm_t comm = nullptr;
     int rank = 0, world = 1;
     bool peer_ok = false;
+    bool decode_ok = false;                      // every rank fuses decode layers (peer exchange)
     char *xbuf = nullptr;                        // this rank's exchange buffer
     char *peer_base[slc::k::kMaxPeers] = {};     // every rank's buffer (own = xbuf)
     size_t data_bytes = 0, flag_bytes = 0;
+    size_t dec_data_off = 0, dec_count_off = 0;   // the persistent decode kernel's words, launch count
 };
 
 namespace {
@@ -83,6 +85,12 @@ void release_peers(CommState *c) {
     for (auto &b : c->peer_base) b = nullptr;
     c->xbuf = nullptr;
     c->peer_ok = false;
+    c->decode_ok = false;
+}
+
+bool decode_fusion_requested() {
+    const char *e = getenv("SLC_DECODE_FUSION");
+    return !(e && e[0] == '0');
 }
 
 bool peer_exchange_requested() {
@@ -97,7 +105,12 @@ void setup_peers(slc_device *d, CommState *c) {
     if (c->world < 2 || c->world > slc::k::kMaxPeers) return;
     c->data_bytes = 2 * (size_t)c->world * kXRows * kXHidden * sizeof(float);
     c->flag_bytes = 2 * (size_t)c->world * kXRows * sizeof(uint32_t);
-    const size_t total = c->data_bytes + c->flag_bytes + kXRows * sizeof(uint32_t);
+    // Then the persistent decode kernel's region: words [2][world][kDlTpHidden]
+    // of {f32, epoch} (decode_layers.cu) and this rank's count of fused
+    // decode launches.
+    c->dec_data_off = (c->data_bytes + c->flag_bytes + kXRows * sizeof(uint32_t) + 255) / 256 * 256;
+    c->dec_count_off = c->dec_data_off + 2 * (size_t)c->world * slc::k::kDlTpHidden * sizeof(uint64_t);
+    const size_t total = c->dec_count_off + 16;
     bool ok = peer_exchange_requested() && cudaMalloc(&c->xbuf, total) == cudaSuccess &&
               cudaMemset(c->xbuf, 0, total) == cudaSuccess &&
               cudaDeviceSynchronize() == cudaSuccess;
@@ -129,19 +142,22 @@ void setup_peers(slc_device *d, CommState *c) {
         c->peer_base[p] = static_cast<char *>(ptr);
     }
     cudaGetLastError();
-    // Agreement: on only if every rank succeeded.
-    int32_t flag = ok ? 1 : 0;
+    // Agreement: on only if every rank succeeded (2: every rank also fuses
+    // decode layers, whose exchanges must then happen on all ranks alike).
+    int32_t flag = ok ? (decode_fusion_requested() ? 3 : 1) : 0;
     int32_t *df = reinterpret_cast<int32_t *>(dh);
     const bool agreed =
         cudaMemcpyAsync(df, &flag, 4, cudaMemcpyHostToDevice, d->stream) == cudaSuccess &&
         a.all_reduce(df, df, 1, ncclInt32, ncclMin, c->comm, d->stream) == ncclSuccess &&
         cudaMemcpyAsync(&flag, df, 4, cudaMemcpyDeviceToHost, d->stream) == cudaSuccess &&
-        cudaStreamSynchronize(d->stream) == cudaSuccess && flag == 1;
+        cudaStreamSynchronize(d->stream) == cudaSuccess && flag >= 1;
     cudaGetLastError();
-    if (agreed)
+    if (agreed) {
         c->peer_ok = true;
-    else
+        c->decode_ok = flag == 3;
+    } else {
         release_peers(c);
+    }
 }
 
 }  // namespace
@@ -161,6 +177,25 @@ bool comm_peer_args(slc_device *d, slc::k::PeerReduceArgs *a) {
     a->max_rows = kXRows;
     a->max_hidden = kXHidden;
     return true;
+}
+
+bool comm_decode_peers(slc_device *d, slc::k::DlPeers *out) {
+    CommState *c = d ? d->comm : nullptr;
+    if (!c || !c->peer_ok || !c->decode_ok) return false;
+    out->rank = c->rank;
+    out->world = c->world;
+    for (int p = 0; p < c->world; p++)
+        out->words[p] = reinterpret_cast<uint64_t *>(c->peer_base[p] + c->dec_data_off);
+    out->launches = reinterpret_cast<uint32_t *>(c->xbuf + c->dec_count_off);
+    return true;
+}
+
+extern "C" int slc_comm_peer_status(const slc_device *d, int *peer_allreduce, int *decode_fusion) {
+    if (!d) return SLC_ERR_EXECUTION;
+    const CommState *c = d->comm;
+    if (peer_allreduce) *peer_allreduce = c && c->peer_ok ? 1 : 0;
+    if (decode_fusion) *decode_fusion = c && c->peer_ok && c->decode_ok ? 1 : 0;
+    return SLC_OK;
 }
 
 extern "C" int slc_comm_unique_id(uint8_t out_id[128]) {

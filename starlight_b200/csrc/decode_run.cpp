@@ -249,6 +249,31 @@ bool run_is_sequential(const BlockMember *c, size_t layers, const Match &m) {
     return true;
 }
 
+// Tensor parallelism: a layer is 18 commands, an in-place AllReduce of the o
+// projection's output after command 11 and of the SwiGlu output after
+// command 15 (the lowering's row-parallel projections). The layers at
+// c[0..n) with both all-reduces where they belong, copied without them (the
+// persistent kernel performs them), into `out`.
+constexpr int kTpLayerCmds = kLayerCmds + 2;
+
+bool all_reduce_of(const BlockMember &ar, const BlockMember &producer) {
+    return ar.op->code == SLC_OP_EXT_ALL_REDUCE && ar.n_in == 1 && ar.n_scalars == 0 &&
+           same_ref(ar.in[0], producer.out[0]) && ar.iv[0].dtype == SLC_F32;
+}
+
+void strip_all_reduces(const BlockMember *c, size_t n, std::vector<BlockMember> *out) {
+    out->clear();
+    for (size_t b = 0; b + kTpLayerCmds <= n && out->size() < 128 * (size_t)kLayerCmds;
+         b += kTpLayerCmds) {
+        const BlockMember *l = c + b;
+        if (l[11].op->code != SLC_OP_MATMUL_NT || l[15].op->code != SLC_OP_SWIGLU ||
+            !all_reduce_of(l[12], l[11]) || !all_reduce_of(l[16], l[15]))
+            break;
+        for (int i = 0; i < kTpLayerCmds; i++)
+            if (i != 12 && i != 16) out->push_back(l[i]);
+    }
+}
+
 // Matches as many layers as possible at c[0..n).
 size_t match_run(slc_device *d, const BlockMember *c, size_t n, Match *m) {
     size_t layers = 0;
@@ -339,16 +364,32 @@ void decode_run_invalidate(slc_device *d) {
     d->decode->next_slot = 1;
 }
 
+// Tensor parallelism of the device (world 1: none); false when the device
+// is tensor-parallel but the persistent kernel's exchange is off.
+bool run_peers(slc_device *d, slc::k::DlPeers *tp) {
+    *tp = slc::k::DlPeers{};
+    int rank = 0, world = 1;
+    if (d->comm) slc_comm_world(d, &rank, &world);
+    if (world <= 1) return true;
+    return comm_decode_peers(d, tp);
+}
+
 size_t decode_run_match(slc_device *d, const BlockMember *cmds, size_t n) {
-    if (!d->decode || d->decode->disabled) return 0;
-    if (d->comm) {  // tensor parallelism: the run has collectives between layers
-        int rank = 0, world = 1;
-        slc_comm_world(d, &rank, &world);
-        if (world > 1) return 0;
+    if (!d->decode || (d->decode->disabled && !d->comm)) return 0;
+    slc::k::DlPeers tp;
+    if (!run_peers(d, &tp)) return 0;
+    // Under tensor parallelism every rank decided alike at slc_comm_init.
+    if (tp.world == 1 && d->decode->disabled) return 0;
+    std::vector<BlockMember> stripped;
+    if (tp.world > 1) {
+        strip_all_reduces(cmds, n, &stripped);
+        cmds = stripped.data();
+        n = stripped.size();
     }
     Match m;
     const size_t layers = match_run(d, cmds, n, &m);
     if (layers == 0) return 0;
+    m.run.tp = tp;
     m.run.layers = (uint32_t)layers;
     m.run.layer = m.io.data();
     m.run.x0 = fptr(d, m.x0);
@@ -358,17 +399,29 @@ size_t decode_run_match(slc_device *d, const BlockMember *cmds, size_t n) {
         slc::k::decode_layers_scratch_bytes(m.run) > ws_scratch_bytes(d) ||
         slc::k::decode_layers_image_bytes((int)layers) > kImageSlotBytes)
         return 0;
-    return layers * kLayerCmds;
+    return layers * (tp.world > 1 ? kTpLayerCmds : kLayerCmds);
 }
 
 int decode_run_launch(slc_device *d, const BlockMember *cmds, size_t n, const uint32_t *const *dyn,
                       bool prepare_only, bool *launched) {
     *launched = false;
     DecodeRunState *s = d->decode;
-    if (!s || s->disabled) return SLC_OK;
+    if (!s) return SLC_OK;
+    slc::k::DlPeers tp;
+    if (!run_peers(d, &tp)) return SLC_OK;
+    if (tp.world == 1 && s->disabled) return SLC_OK;
+    const size_t stride = tp.world > 1 ? kTpLayerCmds : kLayerCmds;
+    const size_t n_orig = n;
+    std::vector<BlockMember> stripped;
+    if (tp.world > 1) {
+        strip_all_reduces(cmds, n, &stripped);
+        cmds = stripped.data();
+        n = stripped.size();
+    }
     Match m;
     const size_t layers = match_run(d, cmds, n, &m);
-    if (layers == 0 || layers * kLayerCmds != n) return SLC_OK;
+    if (layers == 0 || layers * stride != n_orig) return SLC_OK;
+    m.run.tp = tp;
     m.run.layers = (uint32_t)layers;
     m.run.layer = m.io.data();
     m.run.x0 = fptr(d, m.x0);
@@ -376,7 +429,7 @@ int decode_run_launch(slc_device *d, const BlockMember *cmds, size_t n, const ui
     m.run.cache = fptr(d, m.kv);
     const bool graph = dyn != nullptr;
     for (size_t l = 0; l < layers; l++) {
-        m.io[l].d_past = graph ? dyn[l * kLayerCmds + 9] : nullptr;
+        m.io[l].d_past = graph ? dyn[l * stride + 9] : nullptr;
         if (graph && !m.io[l].d_past) return SLC_OK;
     }
     if (!slc::k::decode_layers_supported(m.run)) return SLC_OK;

@@ -128,6 +128,9 @@ void release_comm(slc_device *d);
 // Fills the peer-exchange fields of `a` (false when the communicator has no
 // peer exchange: world 1, switched off, or setup failed on some rank).
 bool comm_peer_args(slc_device *d, slc::k::PeerReduceArgs *a);
+// The persistent decode kernel's exchange regions (false: no tensor
+// parallelism, peer mappings off, or decode fusion off on some rank).
+bool comm_decode_peers(slc_device *d, slc::k::DlPeers *out);
 // AllReduce(partial) -> Add(residual, partial) -> RmsNorm(sum), validated:
 // launched as the fused peer-memory kernel when its conditions hold.
 int slc_launch_allreduce_add_rmsnorm(slc_device *d, const BlockMember *ar, const BlockMember *add,

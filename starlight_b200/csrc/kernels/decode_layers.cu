@@ -51,12 +51,15 @@
 //
 // GEMV (the decode GEMV arithmetic of gemv_lane.cu): weights in 16-row
 // tiles; each worker owns a contiguous range of whole tiles (no cross-CTA
-// sums). A tile is streamed in chunks of [16 rows][1 KiB of codes] (one 2-D
-// TMA box, rows padded in shared memory so that neighbouring rows sit 16
-// banks apart) plus the chunk's scales ([16 rows][groups of the chunk], a
-// second box, padded likewise); a worker's tiles go in groups of four,
-// chunk by chunk within a group. Consumer warp w multiplies the 64-byte
-// warp-steps 2w and 2w + 1 of every chunk with the s8 tensor-core path
+// sums). A tile is streamed in chunks of [16 rows][C bytes of codes] (one
+// 2-D TMA box, C chosen per stage by the host, at most 1 KiB; rows padded
+// in shared memory so that neighbouring rows sit 16 banks apart) plus the
+// chunk's scales ([16 rows][groups of the chunk], a second box padded
+// likewise, or for single-chunk rows one bulk copy of the tile's contiguous
+// scale rows); a worker's tiles go in groups of four, chunk by chunk within
+// a group. Consumer warp w multiplies two 64-byte warp-steps of every chunk
+// (2w and 2w + 1 of a 1 KiB chunk, w and w + 8 of a shorter one) with the
+// s8 tensor-core path
 // (INT4 nibbles as 16 x code, activations as three exact 7-bit digits per
 // value in the MMA's N dimension, integer block sums converted exactly and
 // scaled by scale * 2^e * 2^-7d), reusing a chunk's digits for the whole
@@ -141,6 +144,7 @@ struct DlLayer {
     uint32_t past;           // host past_len otherwise
     uint32_t order;          // bit c: the scribe needs a barrier before output c
     float *cmd[kDlCmds];     // command outputs, in command order
+    const float *scales[7];  // scale rows of q k v o gate up down (single-chunk stages)
 };
 
 struct alignas(64) DlArgs {
@@ -157,6 +161,10 @@ struct alignas(64) DlArgs {
     long long par_stride;  // floats from the keys to the values of a cache layer
     long long lay_stride;  // floats between cache layers
     int L, H, Hq, Hkv, I, G, group, gptj, max_seq, W, nchunk_cap;
+    int stC[5];                  // code bytes per chunk of stages kQKV .. kDOWN (host choice)
+    int tp_rank, tp_world;       // tensor parallelism (world 1: none)
+    uint64_t *xwords[kMaxPeers]; // every rank's exchange words [2][world][kDlTpHidden]
+    uint32_t *tp_launches;       // this rank's fused launches so far (exchange epochs)
     int dig_bytes, nch_max;
     int off_bar, off_misc, off_resid, off_dig, off_fx, off_red, off_trig;
     double denom[kD / 2];
@@ -337,6 +345,8 @@ struct StageGeo {
     float *out0, *out1, *out2;  // private outputs
     int tiles, K, rowb, C, nch, wact, gpc;
     int Cp, gps;  // slot row strides: code bytes, scale floats
+    int bulk;     // single-chunk tiles: the scales by one bulk copy of the tile's rows
+    int wstep0, wstride;  // warp w takes warp-steps wstep0 * w and wstep0 * w + wstride
 };
 
 // Slot row strides of a stage with rows of rowb code bytes in chunks of C
@@ -383,12 +393,16 @@ __device__ __forceinline__ StageGeo stage_geo(const DlArgs &p, int st) {
     g.tend1 = g.tend0 + r1 / 16;
     g.tiles = g.tend1 + r2 / 16;
     g.rowb = FMT == 0 ? g.K / 2 : g.K;
-    g.C = g.rowb < kChunk ? g.rowb : kChunk;
-    g.nch = g.rowb / g.C;
+    g.C = p.stC[st];
+    g.nch = (g.rowb + g.C - 1) / g.C;  // the last chunk may be ragged
     g.wact = g.C / 64;
     g.gpc = g.C * (FMT == 0 ? 2 : 1) / p.group;
     g.Cp = slot_code_stride(g.rowb, g.C);
     g.gps = slot_scale_stride(g.rowb, g.C, g.gpc);
+    g.bulk = g.nch == 1;
+    // Sixteen warp-steps a chunk: adjacent pairs; fewer: w and w + 8.
+    g.wstep0 = g.wact == 16 ? 2 : 1;
+    g.wstride = g.wact == 16 ? 1 : 8;
     return g;
 }
 
@@ -508,7 +522,12 @@ __device__ void producer(const DlArgs &p, const Smem sm) {
                         if (!dst) break;
                         uint64_t *bar = &sm.full[(seq - 1) % kSlots];
                         tma_load_2d(dst, cm, ch * (g.C / 8), row, bar, pol);  // u64 units
-                        tma_load_2d(dst + kSlotCode, cm + 1, ch * g.gpc, row, bar, pol);
+                        if (g.bulk)  // the tile's 16 scale rows are contiguous
+                            bulk_g2s(dst + kSlotCode,
+                                     ly.scales[stage_mat(g, m)] + (size_t)row * g.gpc,
+                                     (uint32_t)(16 * g.gpc * 4), bar, pol);
+                        else
+                            tma_load_2d(dst + kSlotCode, cm + 1, ch * g.gpc, row, bar, pol);
                     }
                 }
             }
@@ -724,14 +743,14 @@ __device__ __forceinline__ void fetch_digits(const DlArgs &p, const Smem &sm,
 
 // ---- consumers: GEMV over this worker's tiles -----------------------------------
 //
-// Warp w multiplies the adjacent warp-steps 2w and 2w + 1 (64 code bytes each)
-// of every chunk. A worker's tiles are streamed in groups of kRedTiles tiles,
+// Warp w multiplies two warp-steps (64 code bytes each) of every chunk
+// (StageGeo::wstep0, wstride). A worker's tiles are streamed in groups of kRedTiles tiles,
 // chunk by chunk within a group, so a warp loads a chunk's digit fragments
 // and factors once and uses them for every tile of the group; each tile
 // keeps its own row sums in registers (chunks added in ascending order).
 
-// The digit fragments (B operands) and factors of warp-steps ws0 and ws0 + 1
-// of the stage input, from the shared digit vector.
+// The digit fragments (B operands) and factors of warp-steps ws0 and
+// ws0 + dstep of the stage input, from the shared digit vector.
 template <int FMT>
 struct StepDigits {
     uint2 bf[2][Q<FMT>::kJ];
@@ -739,13 +758,13 @@ struct StepDigits {
 };
 
 template <int FMT>
-__device__ __forceinline__ void load_step_digits(const unsigned char *rec0, bool has0, bool has1,
-                                                 StepDigits<FMT> &d) {
+__device__ __forceinline__ void load_step_digits(const unsigned char *rec0, int dstep, bool has0,
+                                                 bool has1, StepDigits<FMT> &d) {
     constexpr int WSB = Q<FMT>::kWsb;
     const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        const unsigned char *rec = rec0 + h * Rec<FMT>::kBytes;
+        const unsigned char *rec = rec0 + h * dstep * Rec<FMT>::kBytes;
         const bool on = h == 0 ? has0 : has1;
         const int8_t *cell = reinterpret_cast<const int8_t *>(rec) + gq * WSB + t * 8;
 #pragma unroll
@@ -765,14 +784,14 @@ struct SlotLoad {
 };
 
 __device__ __forceinline__ void load_slot(const unsigned char *sl, int Cp, int gps, int ws0,
-                                          int gi0, int gi1, bool has1, SlotLoad &x) {
+                                          int dstep, int gi0, int gi1, bool has1, SlotLoad &x) {
     const int lane = threadIdx.x & 31, gq = lane >> 2, t = lane & 3;
     const unsigned char *ra = sl + gq * Cp + ws0 * 64 + t * 16;
     const unsigned char *rb = ra + 8 * Cp;
     x.wa[0] = lds128(ra);
     x.wb[0] = lds128(rb);
-    x.wa[1] = has1 ? lds128(ra + 64) : make_uint4(0u, 0u, 0u, 0u);
-    x.wb[1] = has1 ? lds128(rb + 64) : make_uint4(0u, 0u, 0u, 0u);
+    x.wa[1] = has1 ? lds128(ra + dstep * 64) : make_uint4(0u, 0u, 0u, 0u);
+    x.wb[1] = has1 ? lds128(rb + dstep * 64) : make_uint4(0u, 0u, 0u, 0u);
     const float *sc = reinterpret_cast<const float *>(sl + kSlotCode);
     x.s[0][0] = sc[gq * gps + gi0];
     x.s[0][1] = sc[(gq + 8) * gps + gi0];
@@ -849,11 +868,12 @@ __device__ __forceinline__ void gemv_tiles(const DlArgs &p, const Smem &sm, cons
     const int t0 = (int)((long long)c * g.tiles / p.W);
     const int t1 = (int)((long long)(c + 1) * g.tiles / p.W);
     const unsigned char *digv = reinterpret_cast<const unsigned char *>(sm.dig);
-    const int ws0 = 2 * warp;  // the warp's warp-steps of a chunk: ws0, ws0 + 1
-    const int gi0 = ws0 * Q<FMT>::kStep / p.group, gi1 = (ws0 + 1) * Q<FMT>::kStep / p.group;
+    // The warp's warp-steps of a chunk: ws0 and ws0 + dstep.
+    const int ws0 = g.wstep0 * warp, dstep = g.wstride;
+    const int gi0 = ws0 * Q<FMT>::kStep / p.group, gi1 = (ws0 + dstep) * Q<FMT>::kStep / p.group;
     uint32_t *const err = p.err;
     const int nch = g.nch, wact = g.wact, Cp = g.Cp, gps = g.gps;
-    const bool has0 = ws0 < wact, has1 = ws0 + 1 < wact;
+    const int steps = g.rowb / 64;  // warp-steps of a row (a ragged last chunk has fewer)
     static_assert(kRedTiles % 2 == 0, "slot pairs");
     for (int tg = t0; tg < t1; tg += kRedTiles) {
         const int nb = min(kRedTiles, t1 - tg);
@@ -861,16 +881,19 @@ __device__ __forceinline__ void gemv_tiles(const DlArgs &p, const Smem &sm, cons
 #pragma unroll
         for (int b = 0; b < kRedTiles; b++) res[b][0] = res[b][1] = res[b][2] = res[b][3] = 0.f;
         for (int ch = 0; ch < nch; ch++) {
+            const int wv = min(wact, steps - ch * wact);  // this chunk's warp-steps
+            const bool has0 = ws0 < wv, has1 = ws0 + dstep < wv;
             StepDigits<FMT> d;
-            load_step_digits<FMT>(digv + (ch * wact + ws0) * Rec<FMT>::kBytes, has0, has1, d);
+            load_step_digits<FMT>(digv + (ch * wact + ws0) * Rec<FMT>::kBytes, dstep, has0, has1,
+                                  d);
 #pragma unroll
             for (int b = 0; b < kRedTiles; b++) {
                 if (b < nb) {
                     if (wait_full(err, sm, seq)) {
                         if (has0) {
                             SlotLoad x;
-                            load_slot(sm.ring + (seq % kSlots) * kSlotBytes, Cp, gps, ws0, gi0,
-                                      gi1, has1, x);
+                            load_slot(sm.ring + (seq % kSlots) * kSlotBytes, Cp, gps, ws0,
+                                      dstep, gi0, gi1, has1, x);
                             int a[2][4];
                             mma_slot<FMT>(x, d, a);
                             scale_slot<FMT>(x, a, d, has1, res[b]);
@@ -1404,6 +1427,80 @@ __device__ __forceinline__ void attention_item(const DlArgs &p, const Smem &sm, 
     cons_sync();
 }
 
+// ---- consumers: tensor-parallel all-reduce of a row-parallel stage ---------------
+//
+// Under tensor parallelism the o and down GEMVs produce partial sums over
+// this rank's columns. Every rank uses the same tile partition, so CTA c
+// owns the same output rows on every rank. Each value travels as one 8-byte
+// word {float bits, exchange epoch} (an aligned 8-byte store is single-copy
+// atomic, so a word that carries the current epoch carries its value): CTA
+// c stores its rows into its slot in every peer's exchange region (plain
+// NVLink stores, no fence, no separate flag), then polls (bounded) the
+// peers' words for its rows in its own region and adds the ranks' partials
+// in rank order (identical bits on every rank). Slots alternate by epoch
+// parity: a rank writes a slot again two exchanges later, after it has
+// received every peer's words of the exchange in between, which each peer
+// sends only after it has read the slot.
+
+__device__ __forceinline__ void st_u64(uint64_t *a, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t *a) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+    return v;
+}
+
+__device__ __noinline__ void tp_reduce_rows(const DlArgs &p, const Smem &sm, float *out, int r0,
+                                            int r1, uint32_t epoch) {
+    const int tid = threadIdx.x, world = p.tp_world, rank = p.tp_rank;
+    const int par = (int)(epoch & 1u);
+    const int n = r1 - r0;  // at most kConsThreads (checked on the host): one row a thread
+    if (n == 0 || *sm.abort) return;  // the same CTA of every rank has no rows
+    const size_t slot = (size_t)kDlTpHidden;  // words per (parity, source rank)
+    float own = 0.f, acc = 0.f;
+    bool ok = true;
+    if (tid < n) {
+        // This CTA's row of the partial (written before the CTA barrier that
+        // ended the GEMV) into every peer's slot for this rank.
+        own = out[r0 + tid];
+        const uint64_t w = ((uint64_t)epoch << 32) | __float_as_uint(own);
+        for (int q = 0; q < world; q++)
+            if (q != rank)
+                st_u64(p.xwords[q] + ((size_t)par * world + rank) * slot + r0 + tid, w);
+        // The peers' words for the row, added in rank order.
+        for (int q = 0; q < world; q++) {
+            float v = own;
+            if (q != rank) {
+                const uint64_t *src = p.xwords[rank] + ((size_t)par * world + q) * slot + r0 + tid;
+                uint64_t x = ld_relaxed_sys_u64(src);
+                if ((uint32_t)(x >> 32) != epoch && ok) {
+                    const uint64_t t0 = global_ns();
+                    while ((uint32_t)((x = ld_relaxed_sys_u64(src)) >> 32) != epoch) {
+                        if (*sm.abort ||
+                            *reinterpret_cast<volatile unsigned *>(p.sync + kSyncAbort)) {
+                            ok = false;
+                            break;
+                        }
+                        if (global_ns() - t0 > kWaitNs) {
+                            report_error(p.err, kErrWaitTimeout);
+                            atomicExch(p.sync + kSyncAbort, 1u);
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+                v = __uint_as_float((uint32_t)x);
+            }
+            acc = __fadd_rn(acc, v);
+        }
+    }
+    if (!ok) *sm.abort = 1;
+    cons_sync();
+    if (!*sm.abort && tid < n) out[r0 + tid] = acc;
+}
+
 // ---- consumers: the layer program --------------------------------------------------
 //
 // The scribe's phases, counted by the scribe word: S1(l) = 4l (the previous
@@ -1493,6 +1590,10 @@ __device__ void worker_program(const DlArgs &p, const Smem &sm) {
     const unsigned *sc = p.sync + kSyncScribe;
     const int QD = p.Hq * kD;
     unsigned seq = 0, fetches = 0;
+    // Launches before this one (advanced at the end of every launch; the
+    // same count on every rank): numbers this launch's exchanges.
+    const unsigned launch =
+        p.tp_world > 1 ? *reinterpret_cast<volatile unsigned *>(p.tp_launches) : 0u;
     load_smem(sm.resid, p.x0, p.H);
     cons_sync();
     for (int l = 0; l < p.L; l++) {
@@ -1554,6 +1655,13 @@ __device__ void worker_program(const DlArgs &p, const Smem &sm) {
             fetch_digits<FMT>(p, sm, dsrc, K, fetches);
             const StageGeo g = stage_geo<FMT>(p, st);
             gemv_tiles<FMT>(p, sm, g, seq);
+            if (p.tp_world > 1 && (st == kO || st == kDOWN)) {
+                // The rows' partial sums over this rank's columns, all-reduced.
+                const int t0 = (int)((long long)blockIdx.x * g.tiles / p.W);
+                const int t1 = (int)((long long)(blockIdx.x + 1) * g.tiles / p.W);
+                tp_reduce_rows(p, sm, g.out0, 16 * t0, 16 * t1,
+                               launch * 256u + 2u * (unsigned)l + (st == kDOWN ? 2u : 1u));
+            }
             arrive(ctr + (st == kQKV ? cQKV : st == kO ? cO : st == kGU ? cGU : cDOWN));
         }
     }
@@ -1599,7 +1707,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
             for (int l = 0; l < p.L && l < 2; l++)
                 for (int m = 0; m < 7; m++) {
                     prefetch_tensormap(p.maps + p.layers[l].map[m]);
-                    prefetch_tensormap(p.maps + p.layers[l].map[m] + 1);
                 }
             producer<FMT>(p, sm);
         }
@@ -1617,6 +1724,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
         if (ticket == gridDim.x - 1) {  // every CTA is past its last wait
             for (int i = 0; i < kSyncStages + kCtrs * p.L; i++)
                 *reinterpret_cast<volatile unsigned *>(p.sync + i) = 0u;
+            if (p.tp_world > 1) *p.tp_launches += 1u;
             reinterpret_cast<unsigned long long *>(p.sync + kDecodeStampWord)[1] = global_ns();
             __threadfence();
         }
@@ -1633,16 +1741,36 @@ struct Layout {
 
 int rowb_of(int fmt, size_t K) { return (int)(fmt == 0 ? K / 2 : K); }
 
-bool stage_ok(int fmt, size_t K, size_t group, int *nch) {
+// Code bytes per chunk of a stage whose rows hold K codes (0: the stage is
+// not supported): the whole row when it fits one chunk (its scales then come
+// by one bulk copy of the tile's contiguous scale rows), else the largest
+// multiple of 128 bytes up to 1 KiB that divides the row and whose scale
+// groups start 16-byte aligned (the scales' TMA box).
+int chunk_bytes(int fmt, size_t K, size_t group) {
     const int kstep = fmt == 0 ? 128 : 64;
     if (K == 0 || K % (size_t)kstep != 0 || group % (size_t)kstep != 0 || K % group != 0)
-        return false;
+        return 0;
     const int rowb = rowb_of(fmt, K);
-    const int C = rowb < kChunk ? rowb : kChunk;
-    if (rowb % C != 0 || C % 64 != 0) return false;
-    const int gpc = C * (fmt == 0 ? 2 : 1) / (int)group;
-    if (gpc < 4 || gpc % 4 != 0 || gpc > 16 || (K / group) % 4 != 0) return false;
-    *nch = rowb / C;
+    const int groups = (int)(K / group);
+    if (rowb <= kChunk)
+        return rowb % 64 == 0 && 16 * groups * 4 <= kSlotBytes - kSlotCode ? rowb : 0;
+    if (groups % 4 != 0) return 0;  // the scales' row stride (TMA) is a multiple of 16 bytes
+    // 1 KiB chunks, the last one ragged (the boxes read zero fill past the
+    // row's end; its missing warp-steps are skipped).
+    const int gpc1k = kChunk * (fmt == 0 ? 2 : 1) / (int)group;
+    if (gpc1k >= 4 && gpc1k % 4 == 0 && gpc1k <= 16) return kChunk;
+    for (int C = kChunk; C >= 128; C -= 128) {
+        if (rowb % C != 0) continue;
+        const int gpc = C * (fmt == 0 ? 2 : 1) / (int)group;
+        if (gpc >= 4 && gpc % 4 == 0 && gpc <= 16) return C;
+    }
+    return 0;
+}
+
+bool stage_ok(int fmt, size_t K, size_t group, int *nch) {
+    const int C = chunk_bytes(fmt, K, group);
+    if (C == 0) return false;
+    *nch = (rowb_of(fmt, K) + C - 1) / C;
     return true;
 }
 
@@ -1739,6 +1867,17 @@ bool decode_layers_supported(const DlRun &r) {
         return false;
     const Layout L = layout_for(r, sms);
     if (L.smem == 0 || L.smem > (size_t)kSmemLimit || !aligned16(r.x0)) return false;
+    // Tensor parallelism: every rank's exchange region mapped, one flag per
+    // CTA, the hidden row within a slot.
+    if (r.tp.world > 1) {
+        if (r.tp.world > kMaxPeers || r.tp.rank < 0 || r.tp.rank >= r.tp.world ||
+            r.hidden > (uint32_t)kDlTpHidden ||
+            16 * ((r.hidden / 16 + (sms - 1) - 1) / (sms - 1)) > (uint32_t)kConsThreads)
+            return false;  // a worker's rows of o / down: one a consumer thread
+        for (int q = 0; q < r.tp.world; q++)
+            if (!r.tp.words[q] || !aligned16(r.tp.words[q])) return false;
+        if (!r.tp.launches) return false;
+    }
     // The scribe stages q, k and v in its (idle) ring.
     if (((size_t)r.heads + 2 * r.kv_heads) * kD * 4 > (size_t)kSlots * kSlotBytes) return false;
     const size_t H = r.hidden, QD = r.heads * kD, KD = r.kv_heads * kD, I = r.inter;
@@ -1774,18 +1913,24 @@ bool decode_layers_image(const DlRun &r, void *host_image, size_t bytes, const v
         for (int m = 0; m < 7; m++) {
             const QuantWeight &w = io.w[m];
             const int rowb = (int)w.row_bytes;
-            const int C = rowb < kChunk ? rowb : kChunk;
+            const int C = chunk_bytes(r.format, w.k, r.group);
+            if (C == 0) return false;
             const int gpc = C * (r.format == 0 ? 2 : 1) / (int)r.group;
             const int idx = (int)(l * 14 + 2 * m);
             // Boxes of the slot row strides (codes in 8-byte units: a padded
             // row of 1088 bytes is 136 elements, within the 256 a box allows).
+            // Single-chunk rows take their scales by bulk copy (no map).
             const int Cp = slot_code_stride(rowb, C), gps = slot_scale_stride(rowb, C, gpc);
             if (!encode_tensor_map_2d(&maps[idx], CU_TENSOR_MAP_DATA_TYPE_UINT64, w.codes,
                                       (uint64_t)rowb / 8, w.n, (uint64_t)rowb, (uint32_t)Cp / 8,
-                                      16) ||
-                !encode_tensor_map_2d(&maps[idx + 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, w.scales,
-                                      w.groups, w.n, w.groups * 4, (uint32_t)gps, 16))
+                                      16))
                 return false;
+            memset(&maps[idx + 1], 0, sizeof(CUtensorMap));
+            if (rowb > C && !encode_tensor_map_2d(&maps[idx + 1], CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                                  w.scales, w.groups, w.n, w.groups * 4,
+                                                  (uint32_t)gps, 16))
+                return false;
+            d.scales[m] = w.scales;
             d.map[m] = idx;
         }
         d.cache_layer = (int)io.cache_layer;
@@ -1882,6 +2027,15 @@ cudaError_t decode_layers(cudaStream_t s, const DlRun &r, const void *dev_image,
     a.max_seq = (int)r.max_seq;
     a.W = sms - 1;
     a.nchunk_cap = L.nchunk_cap;
+    a.stC[kQKV] = chunk_bytes(r.format, r.hidden, r.group);
+    a.stC[kATTN] = 0;
+    a.stC[kO] = chunk_bytes(r.format, qd, r.group);
+    a.stC[kGU] = chunk_bytes(r.format, r.hidden, r.group);
+    a.stC[kDOWN] = chunk_bytes(r.format, r.inter, r.group);
+    a.tp_rank = r.tp.world > 1 ? r.tp.rank : 0;
+    a.tp_world = r.tp.world > 1 ? r.tp.world : 1;
+    for (int q = 0; q < kMaxPeers; q++) a.xwords[q] = q < a.tp_world ? r.tp.words[q] : nullptr;
+    a.tp_launches = a.tp_world > 1 ? r.tp.launches : nullptr;
     a.dig_bytes = L.dig_bytes;
     a.nch_max = L.nch_max;
     a.off_bar = L.off_bar;

@@ -214,6 +214,19 @@ struct DlLayerIo {
     const uint32_t *d_past;    // device past_len (graph replay) or null
     float *cmd[kDlCmds];       // command output buffers
 };
+// Tensor parallelism of a run (world 1: none). The o and down projections
+// hold this rank's columns (partial sums); the kernel all-reduces them over
+// peer memory: words[parity][source rank][kDlTpHidden] of {f32 bits, epoch}
+// in every rank's exchange region, mapped into all ranks (comm.cpp).
+constexpr int kDlTpHidden = 16384;
+struct DlPeers {
+    int rank = 0, world = 1;
+    uint64_t *words[kMaxPeers] = {};
+    // This rank's count of fused launches so far (advanced by the last CTA
+    // of every launch; it lives with the words, so the exchanges' epochs
+    // never repeat while the exchange region exists).
+    uint32_t *launches = nullptr;
+};
 struct DlRun {
     uint32_t layers, hidden, heads, kv_heads, head_dim, inter;
     int format;                // 0 INT4, 1 INT8
@@ -225,6 +238,7 @@ struct DlRun {
     float *cache;              // KV state [1, cache_layers, 2, max_seq, kv_heads, head_dim]
     uint32_t cache_layers, max_seq;
     const DlLayerIo *layer;    // [layers]
+    DlPeers tp;                // heads, kv_heads, inter and the o / down columns are this rank's
 };
 bool decode_layers_supported(const DlRun &r);
 size_t decode_layers_image_bytes(int layers);

@@ -288,6 +288,7 @@ def load_library():
         "slc_comm_unique_id": (C.c_int, [C.POINTER(C.c_uint8)]),
         "slc_comm_init": (C.c_int, [P, C.POINTER(C.c_uint8), C.c_int, C.c_int]),
         "slc_comm_world": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "slc_comm_peer_status": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -307,7 +308,7 @@ def exported_symbols():
             "slc_fill_normal",
             "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture", "slc_flush",
             "slc_capture_stats", "slc_decode_fusion_stats",
-            "slc_comm_unique_id", "slc_comm_init", "slc_comm_world"]
+            "slc_comm_unique_id", "slc_comm_init", "slc_comm_world", "slc_comm_peer_status"]
 
 
 def _ptr(a: np.ndarray):
@@ -468,6 +469,13 @@ class CudaDevice:
         self._check(self._lib.slc_decode_fusion_stats(self._d, C.byref(info)))
         return {"launched": int(info.launched), "refused": int(info.refused),
                 "last_ms": float(info.last_ms)}
+
+    def peer_status(self) -> dict:
+        """Peer-memory paths agreed by all ranks at comm_init: the fused
+        all-reduce + Add + RmsNorm kernel and persistent decode-layer fusion."""
+        a, b = C.c_int(0), C.c_int(0)
+        self._check(self._lib.slc_comm_peer_status(self._d, C.byref(a), C.byref(b)))
+        return {"peer_allreduce": bool(a.value), "decode_fusion": bool(b.value)}
 
     def comm_init(self, unique_id: bytes, rank: int, world: int):
         buf = (C.c_uint8 * 128)(*unique_id)

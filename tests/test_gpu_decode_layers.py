@@ -3,8 +3,9 @@ decode_layers.cu), reached the way the engine reaches it: command capture on,
 batch 1, one token per step, every layer's sixteen commands fused into one
 cooperative launch.
 
-For several model shapes (GQA groups 1, 4 and 8; INT4 and INT8; rows of more
-and of fewer than 1 KiB of codes; a short and a long context, so that the key
+For several model shapes (GQA groups 1, 2, 4 and 8; INT4 and INT8; rows of
+more and of fewer than 1 KiB of codes, and rows whose last 1 KiB chunk is
+ragged; a short and a long context, so that the key
 chunks per kv head vary) every decode step's logits must match the CPU oracle
 (restated backend-cpu kernels on the dequantized weights) within the
 reduction/matmul tolerance, every greedy id must match bit for bit, and the
@@ -29,6 +30,8 @@ SHAPES = {
     "g4_int4": (2048, 16, 4, 6144, orc.INT4, 3),
     "g8_int8": (2048, 16, 2, 4096, orc.INT8, 2),
     "g1_int4_short_rows": (1024, 8, 8, 2048, orc.INT4, 3),
+    # down rows of 1536 code bytes: a 1 KiB chunk and a ragged 512-byte one
+    "g2_int4_ragged_down": (2048, 16, 8, 3072, orc.INT4, 2),
 }
 
 
@@ -85,7 +88,8 @@ def _run(shape, prefill, steps, fused, ref):
 
 
 @pytest.mark.parametrize("shape,prefill", [("g4_int4", 37), ("g4_int4", 300), ("g8_int8", 90),
-                                           ("g1_int4_short_rows", 20)])
+                                           ("g1_int4_short_rows", 20),
+                                           ("g2_int4_ragged_down", 50)])
 def test_fused_decode_layers_match_oracle(shape, prefill):
     steps = 6
     ocfg, _ = _configs(shape, prefill, steps)

@@ -120,7 +120,7 @@ FUSED_CASES = [(1, 4096, True), (2, 512, False), (5, 1024, False), (3, 768, True
 
 def _fused_expected_launches(rows, reuse):
     if reuse and rows > 1:
-        return 3  # NCCL, Add, RmsNorm
+        return 2  # NCCL, then Add + RmsNorm fused (the output takes the input's bytes exactly)
     return 1 if rows <= 32 else 2  # peer-memory kernel, or NCCL + fused Add/RmsNorm
 
 
