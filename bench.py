@@ -273,24 +273,28 @@ def run_reference(args, dist: Dist):
 
 def fused_layer_bytes(cfg, past):
     """Algorithmic HBM bytes of one layer of the persistent decode kernel at
-    one token: the seven quantized matrices (codes + one f32 scale per
-    group), the layer's cached keys and values at positions [0, past) read
-    once and the new position's written, and the two norm weights."""
-    D = cfg.head_dim
-    mats = [(cfg.heads * D, cfg.hidden), (cfg.kv_heads * D, cfg.hidden),
-            (cfg.kv_heads * D, cfg.hidden), (cfg.hidden, cfg.heads * D),
-            (cfg.inter, cfg.hidden), (cfg.inter, cfg.hidden), (cfg.hidden, cfg.inter)]
+    one token, on one rank: the seven quantized matrices (codes + one f32
+    scale per group; q/k/v/gate/up rows and o/down columns split over the
+    tensor-parallel ranks), the rank's cached keys and values at positions
+    [0, past) read once and the new position's written, and the two norm
+    weights."""
+    D, w_ = cfg.head_dim, max(1, cfg.tp_world)
+    hq, hkv, inter = cfg.heads // w_, cfg.kv_heads // w_, cfg.inter // w_
+    mats = [(hq * D, cfg.hidden), (hkv * D, cfg.hidden), (hkv * D, cfg.hidden),
+            (cfg.hidden, hq * D), (inter, cfg.hidden), (inter, cfg.hidden), (cfg.hidden, inter)]
     int4 = int(cfg.quant) == 0
     w = sum((n * k // 2 if int4 else n * k) + 4 * n * (k // cfg.group_size) for n, k in mats)
-    kv = 2 * past * cfg.kv_heads * D * 4 + 2 * cfg.kv_heads * D * 4
+    kv = 2 * past * hkv * D * 4 + 2 * hkv * D * 4
     return w + kv + 2 * cfg.hidden * 4
 
 
 def streamed_weight_bytes(cfg):
     """Quantized weight bytes one decode step streams, per GPU (the layers'
     matrices and the vocabulary projection, split over the TP ranks)."""
-    per_layer = fused_layer_bytes(cfg, 0) - 2 * cfg.kv_heads * cfg.head_dim * 4 - 2 * cfg.hidden * 4
-    return (cfg.layers * per_layer + model_lm_bytes(cfg)) / max(1, cfg.tp_world)
+    w_ = max(1, cfg.tp_world)
+    per_layer = (fused_layer_bytes(cfg, 0) - 2 * (cfg.kv_heads // w_) * cfg.head_dim * 4
+                 - 2 * cfg.hidden * 4)
+    return cfg.layers * per_layer + model_lm_bytes(cfg) / w_
 
 
 def model_lm_bytes(cfg):
@@ -311,8 +315,9 @@ def fused_roofline(cfg, fused_ms, pasts, peak):
     return {"bound": "hbm", "achieved": achieved, "peak": peak[0], "unit": "GB/s",
             "frac": achieved / peak[0],
             "traffic": ratio * per_launch if ratio is not None else None,
-            "kernel": "decode_layers_kernel (persistent, all %d layers of a decode step)"
-                      % cfg.layers,
+            "kernel": ("decode_layers_kernel (persistent, all %d layers of a decode step%s)"
+                       % (cfg.layers, ", this rank's shard, o/down all-reduced in the kernel"
+                          if cfg.tp_world > 1 else "")),
             "algorithmic_bytes_per_launch": per_launch, "launch_us": launch_s * 1e6,
             "launches_timed": len(fused_ms), "peak_source": peak[1],
             "traffic_source": ("ncu dram bytes of a 4-layer launch per algorithmic byte, "
@@ -476,10 +481,15 @@ def run_ours(args, dist: Dist):
     # (at batch 1 without tensor parallelism the layers of a step run as one
     # persistent kernel, which stamps its own start and end on the device).
     dev.set_capture(True)
+    peer = None
     if world > 1:
         uid = comm_unique_id() if rank == 0 else None
         uid = dist.broadcast_bytes(uid, 128)
         dev.comm_init(uid, rank, world)
+        peer = dev.peer_status()
+        if not (peer["peer_allreduce"] and peer["decode_fusion"]) and rank == 0:
+            print("bench: ERROR peer-memory paths off at %d ranks (%s): all-reduces fall back "
+                  "to NCCL" % (world, peer), file=sys.stderr, flush=True)
     B, T = args.batch, args.prompt
     base = LLAMA3_8B if args.model == "8b" else LLAMA2_70B
     layers = base.layers if args.layers == 32 else args.layers
@@ -529,11 +539,10 @@ def run_ours(args, dist: Dist):
         ids = logits.argmax(axis=1).astype(np.uint32)
         wall += time.perf_counter() - w0
         device_ms += model.last_step_ms()
-        if world == 1:
-            fs = dev.decode_fusion_stats()
-            if fs["last_ms"] > 0:
-                fused_ms.append(fs["last_ms"])
-                pasts.append(past)
+        fs = dev.decode_fusion_stats()
+        if fs["last_ms"] > 0:
+            fused_ms.append(fs["last_ms"])
+            pasts.append(past)
         past += 1
     dev.synchronize()
     torch.cuda.nvtx.range_pop()
@@ -546,10 +555,11 @@ def run_ours(args, dist: Dist):
     result = None
     if rank == 0:
         peak = hbm_peak()
-        if world == 1 and len(fused_ms) == args.steps:
+        if len(fused_ms) == args.steps:
             roof = fused_roofline(cfg, fused_ms, pasts, peak)
             roof["step"] = {"achieved": (cfg.layers * statistics.mean(
-                                fused_layer_bytes(cfg, p) for p in pasts) + model_lm_bytes(cfg))
+                                fused_layer_bytes(cfg, p) for p in pasts)
+                                + model_lm_bytes(cfg) / max(1, world))
                             / (device_ms / args.steps / 1e3) / 1e9,
                             "note": "whole decode step: fused layers + final norm + "
                                     "vocabulary projection bytes over the step time"}
@@ -579,6 +589,8 @@ def run_ours(args, dist: Dist):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 2 * 4 * B,
                     "d2h_bytes_per_step": 4 * B * V},
             "gpu_launches": launches,
+            "launches_per_step": launches / args.steps,
+            "peer_paths": peer,
             "capture": dev.capture_stats(),
             "roofline": roof,
             "norm": norm,
