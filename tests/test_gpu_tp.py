@@ -185,7 +185,7 @@ def _fused_rank(rank, world, port, q):
 
 
 @pytest.mark.timeout(300)
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_fused_allreduce_add_rms_norm_matches_commands(world):
     # With capture on, the all-reduce and the Add + RmsNorm after it go out as
     # one peer-memory kernel, over repeated calls (the kernel's per-row epochs
