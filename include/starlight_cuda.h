@@ -303,6 +303,16 @@ int slc_comm_world(const slc_device *device, int *rank, int *world);
  * rank failed to map its peers or set SLC_PEER_ALLREDUCE=0 (both) or
  * SLC_DECODE_FUSION=0 (the second); NCCL carries the all-reduces then. */
 int slc_comm_peer_status(const slc_device *device, int *peer_allreduce, int *decode_fusion);
+/* The communicator's asynchronous error (ncclCommGetAsyncError): SLC_OK while
+ * healthy, SLC_ERR_EXECUTION once NCCL reports a failure or after
+ * slc_comm_abort. */
+int slc_comm_async_error(slc_device *device);
+/* Tears this rank's communicator down without waiting for the other ranks
+ * (ncclCommAbort), e.g. after a host-side check found that a peer left
+ * between steps; captured graphs and peer mappings are dropped, and later
+ * collectives on this device fail with SLC_ERR_EXECUTION instead of waiting
+ * for the missing rank. */
+int slc_comm_abort(slc_device *device);
 
 /* ---- EXTENSION (no counterpart in the reference): quantized matmul that
  * allocates nothing ---------------------------------------------------------

@@ -37,6 +37,8 @@ struct NcclApi {
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
                                cudaStream_t) = nullptr;
     ncclResult_t (*destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*abort)(ncclComm_t) = nullptr;
+    ncclResult_t (*async_error)(ncclComm_t, ncclResult_t *) = nullptr;
     bool ok = false;
 };
 
@@ -55,7 +57,10 @@ NcclApi &api() {
         a.all_reduce = (decltype(a.all_reduce))dlsym(a.handle, "ncclAllReduce");
         a.all_gather = (decltype(a.all_gather))dlsym(a.handle, "ncclAllGather");
         a.destroy = (decltype(a.destroy))dlsym(a.handle, "ncclCommDestroy");
-        a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.all_gather && a.destroy;
+        a.abort = (decltype(a.abort))dlsym(a.handle, "ncclCommAbort");
+        a.async_error = (decltype(a.async_error))dlsym(a.handle, "ncclCommGetAsyncError");
+        a.ok = a.get_unique_id && a.init_rank && a.all_reduce && a.all_gather && a.destroy &&
+               a.abort && a.async_error;
     });
     return a;
 }
@@ -233,6 +238,31 @@ extern "C" int slc_comm_init(slc_device *d, const uint8_t unique_id[128], int ra
     return SLC_OK;
 }
 
+extern "C" int slc_comm_async_error(slc_device *d) {
+    if (!d) return SLC_ERR_EXECUTION;
+    CommState *c = d->comm;
+    if (!c) return SLC_OK;
+    if (!c->comm) return slc_fail(d, SLC_ERR_EXECUTION, "the communicator was aborted");
+    ncclResult_t r = ncclSuccess;
+    if (api().async_error(c->comm, &r) != ncclSuccess || (r != ncclSuccess && r != ncclInProgress))
+        return slc_fail(d, SLC_ERR_EXECUTION, "the communicator reported an asynchronous error");
+    return SLC_OK;
+}
+
+extern "C" int slc_comm_abort(slc_device *d) {
+    if (!d) return SLC_ERR_EXECUTION;
+    CommState *c = d->comm;
+    if (!c || !c->comm) return SLC_OK;
+    cudaSetDevice(d->ordinal);
+    // Captured graphs hold the communicator and the peer mappings.
+    invalidate_capture(d);
+    release_peers(c);
+    api().abort(c->comm);
+    c->comm = nullptr;
+    cudaGetLastError();
+    return SLC_OK;
+}
+
 extern "C" int slc_comm_world(const slc_device *d, int *rank, int *world) {
     if (!d) return SLC_ERR_EXECUTION;
     if (rank) *rank = d->comm ? d->comm->rank : 0;
@@ -244,13 +274,13 @@ void release_comm(slc_device *d) {
     if (!d->comm) return;
     cudaSetDevice(d->ordinal);
     release_peers(d->comm);
-    if (d->comm->comm && api().ok) api().destroy(d->comm->comm);
+    if (d->comm->comm && api().ok) api().destroy(d->comm->comm);  // null after slc_comm_abort
     delete d->comm;
     d->comm = nullptr;
 }
 
 int comm_all_reduce(slc_device *d, float *data, uint64_t count) {
-    if (!d->comm) return SLC_ERR_EXECUTION;
+    if (!d->comm || (d->comm->world > 1 && !d->comm->comm)) return SLC_ERR_EXECUTION;
     if (count == 0 || d->comm->world == 1) return SLC_OK;
     ncclResult_t r = api().all_reduce(data, data, count, ncclFloat32, ncclSum, d->comm->comm,
                                       d->stream);
@@ -259,7 +289,7 @@ int comm_all_reduce(slc_device *d, float *data, uint64_t count) {
 }
 
 int comm_all_gather(slc_device *d, const float *in, float *out, uint64_t rows, uint64_t cols) {
-    if (!d->comm) return SLC_ERR_EXECUTION;
+    if (!d->comm || (d->comm->world > 1 && !d->comm->comm)) return SLC_ERR_EXECUTION;
     const uint64_t world = (uint64_t)d->comm->world;
     if (rows == 0 || cols == 0) return SLC_OK;
     if (world == 1) return slc::k::copy_f32(d->stream, in, out, rows * cols) == cudaSuccess

@@ -289,6 +289,8 @@ def load_library():
         "slc_comm_init": (C.c_int, [P, C.POINTER(C.c_uint8), C.c_int, C.c_int]),
         "slc_comm_world": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "slc_comm_peer_status": (C.c_int, [P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "slc_comm_async_error": (C.c_int, [P]),
+        "slc_comm_abort": (C.c_int, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -308,7 +310,8 @@ def exported_symbols():
             "slc_fill_normal",
             "slc_device_stream", "slc_kernel_launch_count", "slc_set_capture", "slc_flush",
             "slc_capture_stats", "slc_decode_fusion_stats",
-            "slc_comm_unique_id", "slc_comm_init", "slc_comm_world", "slc_comm_peer_status"]
+            "slc_comm_unique_id", "slc_comm_init", "slc_comm_world", "slc_comm_peer_status",
+            "slc_comm_async_error", "slc_comm_abort"]
 
 
 def _ptr(a: np.ndarray):
@@ -476,6 +479,16 @@ class CudaDevice:
         a, b = C.c_int(0), C.c_int(0)
         self._check(self._lib.slc_comm_peer_status(self._d, C.byref(a), C.byref(b)))
         return {"peer_allreduce": bool(a.value), "decode_fusion": bool(b.value)}
+
+    def comm_check(self):
+        """Raises DeviceError if the communicator reported an asynchronous
+        error or was aborted."""
+        self._check(self._lib.slc_comm_async_error(self._d))
+
+    def comm_abort(self):
+        """Tears the communicator down without the other ranks (a peer left):
+        later collectives fail instead of waiting."""
+        self._check(self._lib.slc_comm_abort(self._d))
 
     def comm_init(self, unique_id: bytes, rank: int, world: int):
         buf = (C.c_uint8 * 128)(*unique_id)

@@ -222,3 +222,172 @@ def test_fused_allreduce_add_rms_norm_matches_commands(world):
                     np.testing.assert_allclose(got, eager[ci][0], rtol=1e-5, atol=1e-5)
                 if rep > 0:
                     assert launches == _fused_expected_launches(rows, reuse), (rows, reuse)
+
+
+# ---- failure detection -----------------------------------------------------------
+
+def _skip_rank(rank, world, port, q):
+    # Both ranks run AllReduce -> Add -> RmsNorm (one row) three times under
+    # capture (the peer-memory kernel); then rank 1 skips one call. Rank 0's
+    # kernel waits for rank 1's flag at most 1 s, records the timeout in the
+    # device error word and returns: slc_synchronize reports it, and nothing
+    # is left waiting on the GPU (no NCCL call is involved).
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+    from oracle.pyoracle import Lcg
+    from starlight_b200.device import (BufferRef, CudaDevice, DeviceError, Op, OpCode, Value,
+                                       comm_unique_id)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=120))
+    err = None
+    try:
+        dev = CudaDevice(rank)
+        t = torch.zeros(128, dtype=torch.uint8)
+        if rank == 0:
+            t[:] = torch.frombuffer(bytearray(comm_unique_id()), dtype=torch.uint8)
+        dist.broadcast(t, 0)
+        dev.comm_init(bytes(t.numpy().tobytes()), rank, world)
+        assert dev.peer_status()["peer_allreduce"]
+        dev.set_capture(True)
+        H, F = 4096, Value.f32
+        buf = dev.allocate_f32(4 * H + H)
+        init = np.concatenate([Lcg(5 + rank).normal(H, 0.0, 1.0), Lcg(6).normal(H, 0.0, 1.0),
+                               np.zeros(2 * H, np.float32), Lcg(7).normal(H, 1.0, 0.1)])
+
+        def call():
+            dev.upload_f32(buf, init.astype(np.float32))
+            p, x = BufferRef(buf, 0, H), BufferRef(buf, H, H)
+            s, o, w = BufferRef(buf, 2 * H, H), BufferRef(buf, 3 * H, H), BufferRef(buf, 4 * H, H)
+            dev.dispatch(Op(OpCode.AllReduce), [p], [F((1, H))], [], [])
+            dev.dispatch(Op(OpCode.Add), [x, p], [F((1, H)), F((1, H))], [s], [F((1, H))])
+            dev.dispatch(Op(OpCode.RmsNorm, eps=1e-5), [s, w], [F((1, H)), F((H,))], [o],
+                         [F((1, H))])
+            dev.synchronize()
+
+        for _ in range(3):
+            call()
+        dist.barrier()
+        if rank == 0:
+            t0 = time.time()
+            try:
+                call()
+            except DeviceError as e:
+                err = (str(e), time.time() - t0)
+        dev.close()
+        q.put((rank, err))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, "exception " + repr(e)))
+        raise
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(300)
+def test_fused_allreduce_bounded_wait_reports_timeout():
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_skip_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=240) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs), res
+    assert res[1] is None, res
+    assert res[0] is not None and "bounded wait timed out" in res[0][0], res
+    assert res[0][1] < 10.0, res
+
+
+def _leave_rank(rank, world, port, q):
+    # Rank 1 leaves between steps (after one NCCL all-reduce both ranks ran).
+    # Rank 0 learns it on the host before its next step (RankWatch), aborts
+    # its communicator, and a collective it dispatches afterwards fails at
+    # once instead of waiting for the missing rank.
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from starlight_b200.device import BufferRef, CudaDevice, DeviceError, Op, OpCode, Value
+    from starlight_b200.device import comm_unique_id
+    from starlight_b200.health import RankFailure, RankWatch
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=60))
+    watch = RankWatch(store, rank, world, timeout_s=1.0)
+    out = None
+    try:
+        dev = CudaDevice(rank)
+        if rank == 0:
+            store.set("uid", bytes(comm_unique_id()))
+        uid = store.get("uid")
+        dev.comm_init(uid, rank, world)
+        buf = dev.allocate_f32(1024)
+        dev.upload_f32(buf, np.full(1024, rank + 1.0, np.float32))
+        watch.step(0)
+        dev.dispatch(Op(OpCode.AllReduce), [BufferRef(buf, 0, 1024)], [Value.f32((1, 1024))],
+                     [], [])
+        dev.synchronize()
+        summed = dev.download_f32(buf)
+        if rank == 1:
+            dev.close()
+            q.put((rank, float(summed[0]), None))
+            return
+        failure = None
+        try:
+            watch.step(1)
+        except RankFailure as e:
+            failure = (e.step, e.missing)
+        dev.comm_abort()
+        after = None
+        try:
+            dev.dispatch(Op(OpCode.AllReduce), [BufferRef(buf, 0, 1024)],
+                         [Value.f32((1, 1024))], [], [])
+            dev.synchronize()
+        except DeviceError as e:
+            after = str(e)
+        checked = None
+        try:
+            dev.comm_check()
+        except DeviceError as e:
+            checked = str(e)
+        dev.close()
+        out = (failure, after is not None, checked is not None)
+        q.put((rank, float(summed[0]), out))
+    except Exception as e:
+        q.put((rank, None, "exception " + repr(e)))
+        raise
+    finally:
+        if rank == 0:
+            import time
+            time.sleep(0.5)
+
+
+@pytest.mark.timeout(300)
+def test_rank_leaving_between_steps_is_detected_and_comm_aborted():
+    if _gpus() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leave_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r, (s, o)) for r, s, o in (q.get(timeout=240) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    assert all(p.exitcode == 0 for p in procs), res
+    assert res[1] == (3.0, None), res  # 1 + 2 on both ranks
+    assert res[0][0] == 3.0, res
+    failure, dispatch_failed, check_failed = res[0][1]
+    assert failure == (1, [1]), res
+    assert dispatch_failed and check_failed, res

@@ -74,3 +74,58 @@ def test_shard_plans_and_rank_plumbing(world):
             # Row-parallel shards hold whole quantization groups (group 128).
             if SHARDING[role] == 2:
                 assert shards[0][3] % 128 == 0
+
+
+# ---- rank liveness between steps (starlight_b200/health.py) ---------------------
+
+def _watch_main(rank, world, port, last_step, q):
+    import datetime
+
+    import torch.distributed as dist
+    from starlight_b200.health import RankFailure, RankWatch
+    store = dist.TCPStore("127.0.0.1", port, world, rank == 0,
+                          timeout=datetime.timedelta(seconds=30))
+    watch = RankWatch(store, rank, world, timeout_s=1.0)
+    done, failure = [], None
+    try:
+        for i in range(last_step + 1):
+            watch.step(i)
+            done.append(i)
+    except RankFailure as e:
+        failure = (e.step, e.missing)
+    q.put((rank, done, failure))
+    if rank == 0:  # the store's server lives in rank 0: outlive the others' last use
+        import time
+        time.sleep(0.5)
+
+
+def _run_watch(last_steps):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    world = len(last_steps)
+    procs = [ctx.Process(target=_watch_main, args=(r, world, port, last_steps[r], q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = dict((r, (d, f)) for r, d, f in (q.get(timeout=60) for _ in range(world)))
+    for p in procs:
+        p.join(timeout=30)
+    return res
+
+
+def test_rank_watch_all_ranks_step_together():
+    res = _run_watch([5, 5])
+    for r in range(2):
+        assert res[r] == (list(range(6)), None), res[r]
+
+
+def test_rank_watch_detects_a_rank_that_left_between_steps():
+    # Rank 1 leaves after step 2; rank 0 must learn it before step 3's work,
+    # within the watch's bound, instead of entering a collective that waits.
+    import time
+    t0 = time.time()
+    res = _run_watch([6, 2])
+    assert res[1] == ([0, 1, 2], None), res[1]
+    assert res[0] == ([0, 1, 2], (3, [1])), res[0]
+    assert time.time() - t0 < 30
