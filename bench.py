@@ -599,8 +599,11 @@ def run_ours(args, dist: Dist):
         if world == 1 and not args.no_cpu_baseline:
             threads = os.cpu_count() or 1
             per_token, desc = oracle_decode_sample(B, T, threads)
+            one, _ = oracle_decode_sample(B, T, 1)  # the reference's kernels are single-threaded
             result["cpu_baseline"] = {"value": B / per_token, "unit": "tok/s", "cores": threads,
-                                      "kind": "port", "sample": desc}
+                                      "kind": "port", "sample": desc,
+                                      "single_thread": {"value": B / one, "unit": "tok/s",
+                                                        "cores": 1}}
     model.close()
     dev.close()
     return result
