@@ -57,8 +57,11 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=32)
     ap.add_argument("--warmup", type=int, default=4)
-    ap.add_argument("--batch", type=int, default=1)
-    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="sequences (default: 1 for 8b, 16 for 70b, as BASELINE configs[3], [4])")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="prompt tokens, prefilled before the timed decode (default: 1024 for "
+                         "8b, 2048 for 70b)")
     ap.add_argument("--layers", type=int, default=32, help="(testing only) fewer layers")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--model", default="8b", choices=["8b", "70b"],
@@ -66,13 +69,18 @@ def parse_args(argv=None):
                          "shape INT8 g128 (BASELINE configs[4])")
     ap.add_argument("--synthetic-kv", action="store_true",
                     help="fill the KV cache with N(0,1) values instead of running the prefill "
-                         "(decode cost does not depend on the cached values); default for 70b")
+                         "(decode cost does not depend on the cached values)")
     ap.add_argument("--sweep", action="store_true",
                     help="per-operator and GEMV sweeps of BASELINE configs[1] and [2]")
     ap.add_argument("--gemv", type=str, default=None, metavar="N,K,M",
                     help="profiling aid: only run one quantized MatMulNT shape (INT4 g128, "
                          "random codes) --steps times and print its time")
-    return ap.parse_args(argv)
+    args = ap.parse_args(argv)
+    if args.batch is None:
+        args.batch = 16 if args.model == "70b" else 1
+    if args.prompt is None:
+        args.prompt = 2048 if args.model == "70b" else 1024
+    return args
 
 
 # ---------------------------------------------------------------- helpers --
@@ -500,7 +508,8 @@ def run_ours(args, dist: Dist):
     model.init_random(seed=8, std=0.02)
     V = cfg.vocab
     rng = np.random.default_rng(1234)
-    synthetic_kv = args.synthetic_kv or args.model == "70b"
+    synthetic_kv = args.synthetic_kv
+    prefill_ms = None
     if synthetic_kv:
         # The decode step's cost does not depend on the cached keys/values:
         # fill the cache instead of running the prefill (--synthetic-kv).
@@ -512,6 +521,7 @@ def run_ours(args, dist: Dist):
         prompt = rng.integers(0, V, size=B * T, dtype=np.uint32)
         pos = np.tile(np.arange(T, dtype=np.uint32), B)
         logits = model.step(PREFILL, prompt, pos, T, 0)
+        prefill_ms = dist.max(model.last_step_ms())  # device time, untimed by the bench clock
         ids = logits.argmax(axis=1).astype(np.uint32)
     past = T
     for _ in range(args.warmup):
@@ -590,6 +600,10 @@ def run_ours(args, dist: Dist):
                     "d2h_bytes_per_step": 4 * B * V},
             "gpu_launches": launches,
             "launches_per_step": launches / args.steps,
+            "prefill": None if prefill_ms is None else {
+                "tokens": B * T, "ms": prefill_ms, "tok_s": B * T / (prefill_ms / 1e3),
+                "note": "one prefill step (untimed warm-up of the decode bench), device time, "
+                        "max over ranks; first execution (no graph)"},
             "peer_paths": peer,
             "capture": dev.capture_stats(),
             "roofline": roof,
