@@ -26,7 +26,9 @@
 // Grid: one CTA per SM (all co-resident: cooperative launch). CTAs
 // 0 .. W-1 are workers; CTA W (the last) is the scribe.
 //
-// Stages of a layer (workers), each ended by an arrival counter:
+// Stages of a layer (workers), each ended by an arrival counter (the
+// inputs of the GEMV stages are digitized first: their own arrival counters
+// DQ, DGU, DD separate digitization from use):
 //   QKV   x = x1 + f (previous layer), h = rmsnorm(x); q, k, v GEMVs
 //   ATTN  one (kv head, key chunk) item per worker: RoPE of its q heads and
 //         of the new key, scores over the chunk's keys (cached keys from the
@@ -35,7 +37,11 @@
 //         ascending chunk order by the last CTA of each kv head (ticket)
 //   O     o GEMV on the attention output
 //   GU    x1 = x + o, h2 = rmsnorm(x1); gate and up GEMVs
-//   DOWN  down GEMV on silu(gate) * up (computed while it is staged)
+//   DOWN  down GEMV on silu(gate) * up
+// Under tensor parallelism each rank runs its shard (its heads, gate/up
+// rows and o/down columns); after the O and DOWN GEMVs every worker
+// all-reduces its output rows with the same worker of the other ranks over
+// peer memory (tp_reduce_rows) before the stage's arrival.
 // The residual stream (x, then x1) lives in every CTA's shared memory and
 // is updated redundantly and identically; intermediate activations go
 // through a private scratch area that no command aliases.
@@ -166,7 +172,7 @@ struct alignas(64) DlArgs {
     uint64_t *xwords[kMaxPeers]; // every rank's exchange words [2][world][kDlTpHidden]
     uint32_t *tp_launches;       // this rank's fused launches so far (exchange epochs)
     int dig_bytes, nch_max;
-    int off_bar, off_misc, off_resid, off_dig, off_fx, off_red, off_trig;
+    int off_bar, off_misc, off_resid, off_dig, off_red, off_trig;
     double denom[kD / 2];
 };
 
@@ -178,8 +184,7 @@ struct Smem {
     int *flag;
     float *part;          // [kCons] rms partial sums
     float *resid;         // [H]
-    int8_t *dig;          // [kCons][dig_bytes]
-    float *fx;            // [kCons][2 nch_max][8]
+    int8_t *dig;          // the stage input's digit vector (dig_bytes), or attention scratch
     float *red;           // [kRedTiles][kCons][16]
     float *trig;          // [D]: sin of the D/2 pairs, then cos
 };
@@ -195,7 +200,6 @@ __device__ __forceinline__ Smem carve(const DlArgs &p, unsigned char *base) {
     s.part = reinterpret_cast<float *>(base + p.off_misc + 16);
     s.resid = reinterpret_cast<float *>(base + p.off_resid);
     s.dig = reinterpret_cast<int8_t *>(base + p.off_dig);
-    s.fx = reinterpret_cast<float *>(base + p.off_fx);
     s.red = reinterpret_cast<float *>(base + p.off_red);
     s.trig = reinterpret_cast<float *>(base + p.off_trig);
     return s;
@@ -701,22 +705,6 @@ __device__ __forceinline__ void my_steps(const DlArgs &p, int K, int *s0, int *s
     const int S = K / Q<FMT>::kStep;
     *s0 = (int)((long long)blockIdx.x * S / p.W);
     *s1 = (int)((long long)(blockIdx.x + 1) * S / p.W);
-}
-
-// Global -> shared copy of n16 16-byte units, up to eight loads per thread
-// issued before their stores.
-__device__ __forceinline__ void copy_to_smem(void *dst, const void *src, int n16) {
-    const uint4 *s4 = static_cast<const uint4 *>(src);
-    uint4 *d4 = static_cast<uint4 *>(dst);
-    for (int b = threadIdx.x; b < n16; b += 8 * kConsThreads) {
-        uint4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            if (b + j * kConsThreads < n16) v[j] = __ldcg(s4 + b + j * kConsThreads);
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-            if (b + j * kConsThreads < n16) d4[b + j * kConsThreads] = v[j];
-    }
 }
 
 // The digit vector of a stage input of K values, into shared memory: one
@@ -1734,7 +1722,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_layers_kernel(const __grid
 // ---- host ------------------------------------------------------------------------
 
 struct Layout {
-    int off_bar, off_misc, off_resid, off_dig, off_fx, off_red, off_trig, dig_bytes, nch_max;
+    int off_bar, off_misc, off_resid, off_dig, off_red, off_trig, dig_bytes, nch_max;
     size_t smem;
     int nchunk_cap;
 };
@@ -1807,7 +1795,6 @@ Layout layout_for(const DlRun &r, int sms) {
     off += (size_t)r.hidden * 4;
     L.off_dig = (int)off;
     off += dig_region;
-    L.off_fx = (int)off;  // (unused: digit factors live in the digit records)
     L.off_red = (int)off;
     off += (size_t)kRedTiles * kCons * 16 * 4;
     L.off_trig = (int)off;
@@ -2042,7 +2029,6 @@ cudaError_t decode_layers(cudaStream_t s, const DlRun &r, const void *dev_image,
     a.off_misc = L.off_misc;
     a.off_resid = L.off_resid;
     a.off_dig = L.off_dig;
-    a.off_fx = L.off_fx;
     a.off_red = L.off_red;
     a.off_trig = L.off_trig;
     for (int pr = 0; pr < kD / 2; pr++)
