@@ -625,7 +625,8 @@ def run_ours(args, dist: Dist):
 
 def run_sweep(args):
     """BASELINE configs[1] and [2]: per-operator sweeps (RMSNorm, softmax,
-    SiLU, Mul, residual Add, RoPE at T in {1, 16, 256, 4096, 16384}) and the
+    SiLU, Mul, residual Add, residual Add + broadcast bias, RoPE at T in
+    {1, 16, 256, 4096, 16384}) and the
     quantized matmul sweep (decode GEMV at M in {1, 4, 16}, prefill at M in
     {512, 2048}; INT4 and INT8, group 128). Every case is one captured
     segment of launches over enough distinct input copies to exceed 2x L2,
@@ -675,6 +676,7 @@ def run_sweep(args):
         cases.append(("silu", [T, 14336], 8 * T * 14336))
         cases.append(("mul", [T, 14336], 12 * T * 14336))
         cases.append(("add", [T, H], 12 * T * H))
+        cases.append(("add_bias", [T, H], 12 * T * H + 4 * H))
         cases.append(("rope", [T, 32, 128], 8 * T * 4096 + 4 * T))
         for name, shape, algo in cases:
             n = int(np.prod(shape))
@@ -687,6 +689,8 @@ def run_sweep(args):
                 extra = f32buf(H, (1 + 0.1 * rng.standard_normal(H)).astype(np.float32))
             elif name in ("mul", "add"):
                 extra = f32buf(n, rng.standard_normal(n, dtype=np.float32))
+            elif name == "add_bias":
+                extra = f32buf(n + H, rng.standard_normal(n + H, dtype=np.float32))
             elif name == "rope":
                 extra = dev.allocate_u32(T)
                 dev.upload_u32(extra, np.arange(T, dtype=np.uint32))
@@ -706,6 +710,11 @@ def run_sweep(args):
                     code = OpCode.Mul if name == "mul" else OpCode.Add
                     dev.dispatch(Op(code), [x, BufferRef(extra, 0, n)],
                                  [Value.f32(shape), Value.f32(shape)], [o], [Value.f32(shape)])
+                elif name == "add_bias":  # residual add plus broadcast [H] bias (extension op)
+                    dev.dispatch(Op(OpCode.AddBias),
+                                 [x, BufferRef(extra, 0, n), BufferRef(extra, n, H)],
+                                 [Value.f32(shape), Value.f32(shape),
+                                  Value.f32((H,), ValueRole.Param)], [o], [Value.f32(shape)])
                 else:
                     dev.dispatch(Op(OpCode.Rope, theta=500000.0), [x, BufferRef(extra, 0, T)],
                                  [Value.f32((1, 32, T, 128)), Value.u32((1, T))], [o],

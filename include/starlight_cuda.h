@@ -141,7 +141,12 @@ typedef enum {
      * rank's [rows, cols] F32 input into an output [rows, world * cols]
      * (rank r's block at columns [r*cols, (r+1)*cols)). */
     SLC_OP_EXT_ALL_REDUCE = 0x8000,
-    SLC_OP_EXT_ALL_GATHER = 0x8001
+    SLC_OP_EXT_ALL_GATHER = 0x8001,
+    /* EXTENSION: residual add with a broadcast bias (no sl-ir counterpart;
+     * the benchmark's elementwise sweep): inputs a, b of one shape
+     * [..., cols] and bias [cols]; output of a's shape,
+     * out = (a + b) + bias[col], each sum rounded as f32 (bit-exact). */
+    SLC_OP_EXT_ADD_BIAS = 0x8002
 } slc_opcode;
 
 typedef enum { SLC_ROPE_NEOX = 0, SLC_ROPE_GPTJ = 1 } slc_rope_variant;

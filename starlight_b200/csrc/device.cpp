@@ -159,6 +159,7 @@ bool signature(uint32_t code, Sig *s) {
     case SLC_OP_RMS_NORM_MATMUL: *s = {3, 0, 1, false}; return true;
     case SLC_OP_EXT_ALL_REDUCE: *s = {1, 0, 0, false}; return true;
     case SLC_OP_EXT_ALL_GATHER: *s = {1, 0, 1, false}; return true;
+    case SLC_OP_EXT_ADD_BIAS: *s = {3, 0, 1, false}; return true;
     default: return false;
     }
 }

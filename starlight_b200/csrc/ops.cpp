@@ -625,6 +625,21 @@ int run_op(slc_device *d, const Cmd &c, bool launch) {
         }
         return SLC_OK;
     }
+    case SLC_OP_EXT_ADD_BIAS: {
+        Dims a, b, bias, o;
+        REQUIRE(ck.ivalue(0, &a) && ck.ivalue(1, &b) && ck.ivalue(2, &bias) && ck.ovalue(0, &o));
+        if (!same(a, b) || !same(a, o))
+            return ck.exec("add_bias operands and output must have identical shapes");
+        if (a.rank < 1) return ck.exec("operator requires at least one dimension");
+        uint64_t cols, rows, nb;
+        REQUIRE(ck.last(a, &cols) && ck.product(a, a.rank - 1, &rows));
+        REQUIRE(ck.product(bias, bias.rank, &nb));
+        if (bias.rank != 1 || nb != cols) return ck.exec("add_bias bias must have shape [cols]");
+        const float *ap = ck.f32(0), *bp = ck.f32(1), *zp = ck.f32(2);
+        REQUIRE(ap && bp && zp);
+        if (!launch) return SLC_OK;
+        return finish(ck, k::add_bias(s, ap, bp, zp, ck.output(), rows, cols));
+    }
     case SLC_OP_EXT_ALL_REDUCE: {
         Dims x;
         REQUIRE(ck.ivalue(0, &x));

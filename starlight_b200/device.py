@@ -80,6 +80,7 @@ class OpCode(enum.IntEnum):  # docs/ARCH-0004:226-235, #[repr(u16)] order
     RmsNormMatMul = 17
     AllReduce = 0x8000  # extension: tensor-parallel sum
     AllGather = 0x8001  # extension: tensor-parallel gather of column blocks
+    AddBias = 0x8002  # extension: (a + b) + bias[col], bias broadcast over rows
 
 
 class RopeVariant(enum.IntEnum):

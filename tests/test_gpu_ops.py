@@ -50,6 +50,30 @@ def test_add_mul_scale_bit_exact(dev, n):
     assert np.array_equal(got, orc.scale(a, -1.5))
 
 
+@pytest.mark.parametrize("rows,cols,offset", [(1, 1, 0), (3, 5, 0), (16, 4096, 0), (7, 4096, 1),
+                                              (256, 4096, 0)])
+def test_add_bias_bit_exact(dev, rows, cols, offset):
+    # Extension op (BASELINE configs[1] residual add plus broadcast bias):
+    # (a + b) + bias[col], each sum rounded as f32; an element offset of 1
+    # takes the scalar path.
+    lcg = Lcg(rows * 7 + cols)
+    a, b = lcg.fill(rows * cols, -2, 2), lcg.fill(rows * cols, -2, 2)
+    bias = lcg.fill(cols, -1, 1)
+    abuf = put_f32(dev, np.concatenate([np.zeros(offset, np.float32), a]))
+    ra = BufferRef(abuf.buffer, offset, rows * cols)
+    got = run1(dev, Op(OpCode.AddBias), [ra, put_f32(dev, b), put_f32(dev, bias)],
+               [F((rows, cols)), F((rows, cols)), F((cols,), ValueRole.Param)], (rows, cols))
+    want = ((a.reshape(rows, cols) + b.reshape(rows, cols)).astype(np.float32) + bias).ravel()
+    assert np.array_equal(got, want.astype(np.float32))
+
+
+def test_add_bias_rejects_a_bias_of_the_wrong_length(dev):
+    a = put_f32(dev, np.zeros(8, np.float32))
+    with pytest.raises(DeviceError, match="bias must have shape"):
+        run1(dev, Op(OpCode.AddBias), [a, a, put_f32(dev, np.zeros(3, np.float32))],
+             [F((2, 4)), F((2, 4)), F((3,))], (2, 4))
+
+
 @pytest.mark.parametrize("n", [1, 7, 33, 1 << 18])
 def test_silu(dev, n):
     x = Lcg(n + 1).fill(n, -8, 8)
