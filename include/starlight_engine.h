@@ -65,6 +65,13 @@ void slc_llama_destroy(slc_llama *model);
  * rank's shard, quantized on the device when the config asks for it. */
 int slc_llama_set_weight(slc_llama *model, int role, uint32_t layer, const float *full,
                          uint64_t len);
+/* The same role from already quantized weights in the model's format and
+ * group size (the sl-precision format: payload rows of ceil(K/2) (INT4) or K
+ * bytes, scales [N, ceil(K/group)] f32), full unsharded matrices: this
+ * rank's shard is sliced out (whole rows, or whole groups of columns) and
+ * stored as it is, without quantizing again. */
+int slc_llama_set_quant_weight(slc_llama *model, int role, uint32_t layer, const uint8_t *codes,
+                               uint64_t codes_bytes, const float *scales, uint64_t scales_len);
 /* Synthetic weights generated on the device: matrices and the embedding
  * N(0, std), norm weights N(1, 0.1), one stream per (role, layer) derived
  * from `seed`; element (r, c) of the full matrix is draw r * cols + c, so

@@ -538,6 +538,41 @@ extern "C" int slc_llama_set_weight(slc_llama *m, int role, uint32_t layer, cons
     return rc;
 }
 
+extern "C" int slc_llama_set_quant_weight(slc_llama *m, int role, uint32_t layer,
+                                          const uint8_t *codes, uint64_t codes_bytes,
+                                          const float *scales, uint64_t scales_len) {
+    if (!m || !codes || !scales) return SLC_ERR_EXECUTION;
+    int wi = weight_index(m, role, layer);
+    if (wi < 0) return fail(m, SLC_ERR_EXECUTION, "unknown weight role or layer");
+    Weight &w = m->weights[wi];
+    if (!w.quant) return fail(m, SLC_ERR_EXECUTION, "weight role is not quantized in this model");
+    const bool int4 = m->cfg.quant_format == SLC_QUANT_INT4;
+    const uint64_t g = m->cfg.group_size;
+    auto row_bytes = [&](uint64_t k) { return int4 ? (k + 1) / 2 : k; };
+    const uint64_t full_rb = row_bytes(w.full_cols), full_groups = (w.full_cols + g - 1) / g;
+    if (codes_bytes != w.full_rows * full_rb || scales_len != w.full_rows * full_groups)
+        return fail(m, SLC_ERR_EXECUTION, "quantized weight sizes do not match its role shape");
+    // This rank's shard: whole rows, or whole quantization groups of columns
+    // (checked at creation), so the shard's codes and scales are slices.
+    if (w.col0 % g != 0 || (int4 && w.col0 % 2 != 0))
+        return fail(m, SLC_ERR_EXECUTION, "column shard does not start on a group");
+    const uint64_t rb = row_bytes(w.cols), groups = (w.cols + g - 1) / g;
+    const uint64_t b0 = int4 ? w.col0 / 2 : w.col0, g0 = w.col0 / g;
+    std::vector<uint8_t> payload((w.rows * rb + 3) / 4 * 4, 0);
+    std::vector<float> sc(w.rows * groups);
+    for (uint64_t r = 0; r < w.rows; r++) {
+        memcpy(&payload[r * rb], codes + (w.row0 + r) * full_rb + b0, rb);
+        memcpy(&sc[r * groups], scales + (w.row0 + r) * full_groups + g0, groups * sizeof(float));
+    }
+    slc_device *d = m->dev;
+    if (cudaMemcpyAsync(d->buffers[w.buf].ptr, payload.data(), payload.size(),
+                        cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+        cudaMemcpyAsync(d->buffers[w.scales].ptr, sc.data(), sc.size() * sizeof(float),
+                        cudaMemcpyHostToDevice, d->stream) != cudaSuccess)
+        return fail(m, SLC_ERR_EXECUTION, "host to device copy failed");
+    return slc_synchronize(d);
+}
+
 extern "C" int slc_llama_init_random(slc_llama *m, uint64_t seed, float stdev) {
     if (!m) return SLC_ERR_EXECUTION;
     slc_device *d = m->dev;

@@ -109,6 +109,8 @@ def _bind(lib):
         "slc_llama_create": (C.c_int, [P, C.POINTER(_Config), C.POINTER(P)]),
         "slc_llama_destroy": (None, [P]),
         "slc_llama_set_weight": (C.c_int, [P, C.c_int, C.c_uint32, P, C.c_uint64]),
+        "slc_llama_set_quant_weight": (C.c_int, [P, C.c_int, C.c_uint32, P, C.c_uint64, P,
+                                                 C.c_uint64]),
         "slc_llama_init_random": (C.c_int, [P, C.c_uint64, C.c_float]),
         "slc_llama_step": (C.c_int, [P, C.c_int, P, P, C.c_uint32, C.c_uint32, P, C.c_uint64]),
         "slc_llama_generate": (C.c_int, [P, P, C.c_uint32, P, P]),
@@ -156,6 +158,16 @@ class Llama:
         a = np.ascontiguousarray(full, np.float32).ravel()
         self._check(self._lib.slc_llama_set_weight(self._m, ROLES.index(role), layer,
                                                    C.c_void_p(a.ctypes.data), a.size))
+
+    def set_quant_weight(self, role: str, layer: int, codes: np.ndarray, scales: np.ndarray):
+        """The full (unsharded) weight of `role` as already quantized codes
+        (uint8 rows of the payload) and f32 scales [N, groups] in the model's
+        format and group size; stored as it is (no second quantization)."""
+        c = np.ascontiguousarray(codes, np.uint8).ravel()
+        sc = np.ascontiguousarray(scales, np.float32).ravel()
+        self._check(self._lib.slc_llama_set_quant_weight(self._m, ROLES.index(role), layer,
+                                                         C.c_void_p(c.ctypes.data), c.size,
+                                                         C.c_void_p(sc.ctypes.data), sc.size))
 
     def init_random(self, seed: int, std: float = 0.02):
         self._check(self._lib.slc_llama_init_random(self._m, seed, std))
