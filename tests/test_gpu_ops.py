@@ -68,9 +68,9 @@ def test_add_bias_bit_exact(dev, rows, cols, offset):
 
 
 def test_add_bias_rejects_a_bias_of_the_wrong_length(dev):
-    a = put_f32(dev, np.zeros(8, np.float32))
+    a, b = put_f32(dev, np.zeros(8, np.float32)), put_f32(dev, np.zeros(8, np.float32))
     with pytest.raises(DeviceError, match="bias must have shape"):
-        run1(dev, Op(OpCode.AddBias), [a, a, put_f32(dev, np.zeros(3, np.float32))],
+        run1(dev, Op(OpCode.AddBias), [a, b, put_f32(dev, np.zeros(3, np.float32))],
              [F((2, 4)), F((2, 4)), F((3,))], (2, 4))
 
 
