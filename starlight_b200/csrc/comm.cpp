@@ -15,7 +15,14 @@
 // init, shares its CUDA IPC handle through an NCCL all-gather and maps its
 // peers' buffers; the path is used only when every rank succeeded (agreed by
 // an NCCL min-reduction), otherwise the NCCL all-reduce serves all sizes.
-// SLC_PEER_ALLREDUCE=0 in the environment of any rank switches it off.
+// SLC_PEER_ALLREDUCE=0 in the environment of any rank switches it off. The
+// same buffer holds the persistent decode kernel's exchange words and its
+// launch count; that kernel is used under tensor parallelism only when every
+// rank also allows decode fusion (SLC_DECODE_FUSION, same agreement).
+//
+// Failures: slc_comm_abort tears the communicator down without the other
+// ranks (ncclCommAbort) once a host-side check found that a peer left;
+// slc_comm_async_error polls ncclCommGetAsyncError.
 #include <dlfcn.h>
 #include <nccl.h>
 #include <stdlib.h>

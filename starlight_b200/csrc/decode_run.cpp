@@ -8,7 +8,11 @@
 // (the lowering of docs/ARCH-0006 sections 4-5; operator semantics of
 // crates/backends/backend-cpu/src/device.rs:773-1227) with GroupwiseQuantized
 // weights -- runs as one cooperative launch that leaves every output buffer
-// and the KV state as the commands would.
+// and the KV state as the commands would. Under tensor parallelism a layer
+// is eighteen commands (an in-place AllReduce after MatMulNT o and after
+// SwiGlu); the matcher checks their placement and matches the other
+// sixteen, and the kernel performs the all-reduces over peer memory (only
+// when every rank agreed on it at slc_comm_init).
 //
 // The kernel reads the command buffers only at its start (the first layer's
 // input, weights, norm weights, positions, KV state) and computes from
