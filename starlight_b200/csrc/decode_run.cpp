@@ -486,9 +486,16 @@ int decode_run_launch(slc_device *d, const BlockMember *cmds, size_t n, const ui
         e == cudaErrorCooperativeLaunchTooLarge) {
         // Refused before anything was enqueued (a tensor map the driver does
         // not accept, or one CTA per SM does not fit): the commands run
-        // through the other kernels instead.
+        // through the other kernels instead -- except under tensor
+        // parallelism, where the other ranks' kernels expect this rank's
+        // exchanges and the per-command path would enter collectives they
+        // never join: the step fails here instead (their exchange waits end
+        // with a timeout error).
         cudaGetLastError();
         s->refused++;
+        if (tp.world > 1)
+            return slc_fail(d, SLC_ERR_EXECUTION,
+                            "persistent decode kernel refused under tensor parallelism");
         return SLC_OK;
     }
     if (e != cudaSuccess) {
