@@ -115,17 +115,53 @@ def profile_traffic_ratio(path=TRAFFIC_PROFILE):
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """SM clocks and clock-event (throttle) reasons of this rank's GPU during
+    the timed region, from two sources read together: NVML polled from a
+    thread every 10 ms (a timed region of tens of milliseconds still gets
+    several samples) and `nvidia-smi -lms 200`. Reads only: no clock or other
+    setting of the GPU is changed."""
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    PERIOD_S = 0.010
 
     def __init__(self, index: int):
-        self.index = index
-        self.proc = None
-        self.path = None
+        # NVML and nvidia-smi number the GPUs physically; map this process's
+        # CUDA ordinal through CUDA_VISIBLE_DEVICES when it lists indices.
+        vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        self.index = int(vis[index]) if index < len(vis) and vis[index].isdigit() else index
+        self.proc = self.path = self.thread = None
+        self.rows = []  # (sm_mhz, max_mhz, {reason: bool})
+
+    def _nvml_loop(self, nv, h, stop):
+        bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
+                nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
+        try:
+            mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:
+            return  # the nvidia-smi samples remain
+        while not stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((sm, mx, {n: bool(r & b) for n, b in zip(self.NAMES, bits)}))
+            except Exception:
+                pass
+            stop.wait(self.PERIOD_S)
 
     def start(self):
+        import threading
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, self._stop),
+                                           daemon=True)
+            self.thread.start()
+        except Exception:
+            self.thread = None
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
@@ -136,29 +172,37 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
-    def stop(self):
-        if not self.proc:
-            return None
+    def _smi_rows(self):
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        rows = []
         for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            p = [x.strip() for x in line.split(",")]
+            if len(p) >= 9 and p[1].replace(".", "").isdigit() and p[2].replace(".", "").isdigit():
+                self.rows.append((float(p[1]), float(p[2]),
+                                  {n: v.lower() == "active" for n, v in zip(self.NAMES, p[5:9])}))
         os.unlink(self.path)
+
+    def stop(self):
+        n_nvml = 0
+        if self.thread:
+            self._stop.set()
+            self.thread.join(timeout=5)
+            n_nvml = len(self.rows)
+        if self.proc:
+            self._smi_rows()
+        rows = self.rows
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
-        loaded = [v for v in sm if v > 0.5 * mx] or sm
-        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
-                "reasons": reasons, "samples": len(rows)}
+        mx = max(r[1] for r in rows)
+        reasons = sorted({n for r in rows for n, v in r[2].items() if v})
+        loaded = [r[0] for r in rows if r[0] > 0.5 * mx] or [r[0] for r in rows]
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows),
+                "source": f"{n_nvml} NVML samples every 10 ms, "
+                          f"{len(rows) - n_nvml} nvidia-smi samples every 200 ms"}
 
 
 class Dist:
