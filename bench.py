@@ -134,20 +134,21 @@ class ClockSampler:
         self.proc = self.path = self.thread = None
         self.rows = []  # (sm_mhz, max_mhz, {reason: bool})
 
-    def _nvml_loop(self, nv, h, stop):
+    def _nvml_sample(self, nv, h):
         bits = [nv.nvmlClocksEventReasonHwSlowdown, nv.nvmlClocksEventReasonHwThermalSlowdown,
                 nv.nvmlClocksEventReasonSwThermalSlowdown, nv.nvmlClocksEventReasonSwPowerCap]
         try:
             mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+            r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
         except Exception:
-            return  # the nvidia-smi samples remain
+            return False
+        self.rows.append((sm, mx, {n: bool(r & b) for n, b in zip(self.NAMES, bits)}))
+        return True
+
+    def _nvml_loop(self, nv, h, stop):
         while not stop.is_set():
-            try:
-                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
-                r = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
-                self.rows.append((sm, mx, {n: bool(r & b) for n, b in zip(self.NAMES, bits)}))
-            except Exception:
-                pass
+            self._nvml_sample(nv, h)
             stop.wait(self.PERIOD_S)
 
     def start(self):
@@ -156,6 +157,7 @@ class ClockSampler:
             import pynvml as nv
             nv.nvmlInit()
             h = nv.nvmlDeviceGetHandleByIndex(self.index)
+            self._nv, self._h = nv, h
             self._stop = threading.Event()
             self.thread = threading.Thread(target=self._nvml_loop, args=(nv, h, self._stop),
                                            daemon=True)
@@ -188,6 +190,9 @@ class ClockSampler:
     def stop(self):
         n_nvml = 0
         if self.thread:
+            # One sample as the region ends, taken here: the thread's own
+            # samples can be few when the region lasts only tens of ms.
+            self._nvml_sample(self._nv, self._h)
             self._stop.set()
             self.thread.join(timeout=5)
             n_nvml = len(self.rows)

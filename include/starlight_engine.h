@@ -97,6 +97,12 @@ int slc_llama_weight_ref(const slc_llama *model, int role, uint32_t layer, slc_b
 /* Device time (CUDA events on the device stream) from the first to the last
  * command of the most recent slc_llama_step, in milliseconds. */
 int slc_llama_last_step_ms(const slc_llama *model, float *ms);
+/* Steps (since creation) that relaunched their program's captured graph
+ * directly: with command capture on, once a program's commands have run as
+ * one graph, later steps of that program fill the graph's scalar table
+ * (seq_len, past_len) and relaunch it instead of dispatching every command
+ * again. Results are those of the dispatched step. */
+int slc_llama_memo_steps(const slc_llama *model, uint64_t *count);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -25,6 +25,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <atomic>
 #include <list>
 #include <unordered_map>
 #include <vector>
@@ -50,7 +51,10 @@ struct Graph {
     cudaGraphExec_t exec = nullptr;
     std::vector<unsigned char> key;
     uint64_t launches = 0;  // kernels per replay
+    uint64_t id = 0;        // unique in the process (step memos name graphs by it)
 };
+
+std::atomic<uint64_t> g_next_graph_id{1};
 
 bool dynamic_scalars(uint16_t code) {
     return code == SLC_OP_LAST_TOKEN || code == SLC_OP_KV_APPEND ||
@@ -408,21 +412,33 @@ static int run_pending(slc_device *d, CaptureState *cs, bool dyn) {
     return SLC_OK;
 }
 
-// Copies the segment's dynamic scalars to the device table (stream-ordered).
-static int upload_table(slc_device *d, CaptureState *cs) {
-    if (cs->table_used == 0) return SLC_OK;
-    // The previous copy must have read the pinned table before it changes.
+// The previous table copy must have read the pinned table before it changes.
+static int table_wait(slc_device *d, CaptureState *cs) {
     if (cs->table_pending && cudaEventSynchronize(cs->table_done) != cudaSuccess)
         return slc_fail(d, SLC_ERR_EXECUTION, "capture scalar table synchronization failed");
-    for (const Rec &r : cs->pending)
-        if (r.slot >= 0)
-            memcpy(cs->h_table + r.slot, r.scalars, sizeof(uint32_t) * r.n_scalars);
-    if (cudaMemcpyAsync(cs->d_table, cs->h_table, sizeof(uint32_t) * cs->table_used,
-                        cudaMemcpyHostToDevice, d->stream) != cudaSuccess ||
+    cs->table_pending = false;
+    return SLC_OK;
+}
+
+// Copies slots [0, n) of the pinned table to the device table (stream-ordered).
+static int table_send(slc_device *d, CaptureState *cs, uint32_t n) {
+    if (cudaMemcpyAsync(cs->d_table, cs->h_table, sizeof(uint32_t) * n, cudaMemcpyHostToDevice,
+                        d->stream) != cudaSuccess ||
         cudaEventRecord(cs->table_done, d->stream) != cudaSuccess)
         return slc_fail(d, SLC_ERR_EXECUTION, "capture scalar table upload failed");
     cs->table_pending = true;
     return SLC_OK;
+}
+
+// Copies the segment's dynamic scalars to the device table (stream-ordered).
+static int upload_table(slc_device *d, CaptureState *cs) {
+    if (cs->table_used == 0) return SLC_OK;
+    const int rc = table_wait(d, cs);
+    if (rc != SLC_OK) return rc;
+    for (const Rec &r : cs->pending)
+        if (r.slot >= 0)
+            memcpy(cs->h_table + r.slot, r.scalars, sizeof(uint32_t) * r.n_scalars);
+    return table_send(d, cs, cs->table_used);
 }
 
 static bool try_capture(slc_device *d, CaptureState *cs, Graph *g) {
@@ -462,7 +478,10 @@ static bool try_capture(slc_device *d, CaptureState *cs, Graph *g) {
     return true;
 }
 
-int flush_capture(slc_device *d) {
+// Runs the pending segment (replay, capture or eager); *graph_id names the
+// graph it ran as, 0 when it ran eagerly or failed.
+static int flush_segment(slc_device *d, uint64_t *graph_id) {
+    *graph_id = 0;
     CaptureState *cs = d ? d->capture : nullptr;
     if (!cs || cs->pending.empty()) return SLC_OK;
     cudaSetDevice(d->ordinal);
@@ -489,6 +508,7 @@ int flush_capture(slc_device *d) {
             slc::k::add_launches((int64_t)g.launches);
             cs->stats.replays++;
             cs->stats.replayed_commands += cs->pending.size();
+            *graph_id = g.id;
         }
     } else {
         if (cs->seen.size() > 4096) cs->seen.clear();  // bound the history of keys
@@ -499,6 +519,7 @@ int flush_capture(slc_device *d) {
             g.key = cs->key;
             rc = upload_table(d, cs);
             if (rc == SLC_OK && try_capture(d, cs, &g)) {
+                g.id = g_next_graph_id.fetch_add(1);
                 if (cs->graphs.size() >= kMaxGraphs) {
                     Graph &old = cs->graphs.back();
                     cs->by_hash.erase(key_hash(old.key.data(), old.key.size()));
@@ -514,6 +535,7 @@ int flush_capture(slc_device *d) {
                     slc::k::add_launches((int64_t)ng.launches);
                     cs->stats.captures++;
                     cs->stats.replayed_commands += cs->pending.size();
+                    *graph_id = ng.id;
                 }
                 captured = true;
             } else if (rc == SLC_OK) {
@@ -529,5 +551,99 @@ int flush_capture(slc_device *d) {
     cs->pending.clear();
     cs->key.clear();
     cs->table_used = 0;
+    return rc;
+}
+
+int flush_capture(slc_device *d) {
+    uint64_t graph_id;
+    return flush_segment(d, &graph_id);
+}
+
+// Step memo. A caller that dispatches the same command list every step
+// (an engine program: the same operators on the same buffers, only seq_len
+// and past_len changing) builds the same segment key every time, so the
+// segment always replays the same graph; only the device table of dynamic
+// scalars differs. After a step whose commands were flushed as exactly one
+// segment that ran as a graph, the memo keeps that graph's id and, for every
+// table slot, which of the caller's scalar sources fills it. The next steps
+// then skip dispatching (validating, recording, keying) their commands:
+// they fill the table from the sources and relaunch the graph. Validation is
+// not lost: every check of a command depends only on its buffers, values
+// and the caller's scalars; buffers and quantization bindings cannot change
+// without dropping every graph (which empties the memo: its graph is no
+// longer found), and the scalars' range checks are the caller's, done before
+// each step (seq_len within the program, past_len + seq within the cache).
+// Only on a device without a communicator: a tensor-parallel step keeps the
+// per-command path.
+static std::list<Graph>::iterator memo_graph(CaptureState *cs, const StepMemo *m) {
+    if (!m->graph_id) return cs->graphs.end();
+    for (auto it = cs->graphs.begin(); it != cs->graphs.end(); ++it)
+        if (it->id == m->graph_id) return it;
+    return cs->graphs.end();
+}
+
+bool capture_memo_valid(slc_device *d, const StepMemo *m) {
+    CaptureState *cs = d ? d->capture : nullptr;
+    return cs && !d->comm && cs->pending.empty() && memo_graph(cs, m) != cs->graphs.end();
+}
+
+int capture_memo_replay(slc_device *d, StepMemo *m, const uint32_t *src, size_t n_src) {
+    CaptureState *cs = d->capture;
+    auto it = memo_graph(cs, m);
+    if (it == cs->graphs.end() || !cs->pending.empty())
+        return slc_fail(d, SLC_ERR_EXECUTION, "step memo replayed without its graph");
+    for (uint32_t s : m->slot_src)
+        if (s >= n_src) return slc_fail(d, SLC_ERR_EXECUTION, "step memo scalar source out of range");
+    cudaSetDevice(d->ordinal);
+    const uint32_t n = (uint32_t)m->slot_src.size();
+    int rc = SLC_OK;
+    if (n) {
+        if ((rc = table_wait(d, cs)) != SLC_OK) return rc;
+        for (uint32_t i = 0; i < n; i++) cs->h_table[i] = src[m->slot_src[i]];
+        if ((rc = table_send(d, cs, n)) != SLC_OK) return rc;
+    }
+    cs->graphs.splice(cs->graphs.begin(), cs->graphs, it);
+    Graph &g = cs->graphs.front();
+    if (cudaGraphLaunch(g.exec, d->stream) != cudaSuccess)
+        return slc_fail(d, SLC_ERR_EXECUTION, "CUDA graph launch failed");
+    slc::k::add_launches((int64_t)g.launches);
+    cs->stats.replays++;
+    cs->stats.replayed_commands += m->commands;
+    return SLC_OK;
+}
+
+int capture_flush_memo(slc_device *d, StepMemo *m, const int *src_flat, const uint32_t *src_count,
+                       size_t n_cmds) {
+    m->graph_id = 0;
+    CaptureState *cs = d ? d->capture : nullptr;
+    if (!cs) return flush_capture(d);
+    // Which source fills each table slot, read off the recorded commands
+    // before the flush clears them. Eligible only when the pending segment
+    // is exactly the caller's commands and every scalar is a device-table
+    // scalar (a scalar in the key would make the next step's key differ).
+    bool ok = !d->comm && cs->pending.size() == n_cmds;
+    std::vector<uint32_t> slot_src;
+    if (ok) {
+        slot_src.assign(cs->table_used, UINT32_MAX);
+        size_t off = 0;
+        for (size_t i = 0; i < n_cmds && ok; i++) {
+            const Rec &r = cs->pending[i];
+            if (r.n_scalars != src_count[i] || (r.n_scalars && r.slot < 0)) {
+                ok = false;
+                break;
+            }
+            for (uint32_t j = 0; j < r.n_scalars; j++)
+                slot_src[(size_t)r.slot + j] = (uint32_t)src_flat[off + j];
+            off += src_count[i];
+        }
+        for (uint32_t s : slot_src) ok = ok && s != UINT32_MAX;
+    }
+    uint64_t graph_id;
+    const int rc = flush_segment(d, &graph_id);
+    if (rc == SLC_OK && ok && graph_id) {
+        m->graph_id = graph_id;
+        m->slot_src = std::move(slot_src);
+        m->commands = n_cmds;
+    }
     return rc;
 }

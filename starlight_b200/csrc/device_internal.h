@@ -116,6 +116,24 @@ int slc_launch_attention_block(slc_device *d, const BlockMember *bm, const uint3
 // launched as one kernel when the shapes and buffer reuse allow it.
 int slc_launch_add_rmsnorm(slc_device *d, const BlockMember *add, const BlockMember *rms,
                            bool *launched);
+// Step memo (capture.cpp): lets a caller that dispatches the same command
+// list every step relaunch that list's captured graph without dispatching
+// the commands again; only the dynamic scalars change. Owned by the caller.
+struct StepMemo {
+    uint64_t graph_id = 0;            // 0: empty
+    std::vector<uint32_t> slot_src;   // per device-table slot: index of its scalar source
+    uint64_t commands = 0;
+};
+// True when the memo's graph can be relaunched now.
+bool capture_memo_valid(slc_device *d, const StepMemo *m);
+// Fills the device table from src[0..n_src) and relaunches the memo's graph.
+int capture_memo_replay(slc_device *d, StepMemo *m, const uint32_t *src, size_t n_src);
+// flush_capture, after which the memo holds the flushed segment's graph if
+// the segment was exactly the caller's n_cmds commands (command i taking
+// src_count[i] scalars from sources src_flat[...], in order) and ran as a
+// graph; empty otherwise.
+int capture_flush_memo(slc_device *d, StepMemo *m, const int *src_flat, const uint32_t *src_count,
+                       size_t n_cmds);
 // Try to record a validated command for graph replay. Returns 1 if the
 // command was recorded (launch deferred), 0 if it must be launched now.
 int capture_record(slc_device *d, const slc_op *op, const slc_buffer_ref *in,

@@ -18,6 +18,7 @@
 // section 7); step uploads ids and positions, dispatches every command,
 // synchronizes and downloads the logits. step performs no allocation.
 #include <math.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -64,6 +65,11 @@ struct Program {
     uint64_t scratch_elems = 0;
     std::vector<slc_buffer_ref> refs;
     std::vector<Ready> ready;
+    // The scalar sources of ready[i] are src_flat[sum(src_count[<i]) ...],
+    // src_count[i] of them; the memo relaunches the step's graph directly.
+    std::vector<int> src_flat;
+    std::vector<uint32_t> src_count;
+    StepMemo memo;
 };
 
 uint64_t count_of(const slc_value &v) {
@@ -105,6 +111,8 @@ struct slc_llama {
     std::vector<float> host_logits;
     cudaEvent_t ev_begin = nullptr, ev_end = nullptr;
     float last_step_ms = 0.f;
+    uint64_t memo_steps = 0;  // steps relaunched from a program's step memo
+    bool memo = true;         // SLC_STEP_MEMO=0 at creation: always dispatch
 };
 
 namespace {
@@ -369,6 +377,13 @@ void bind(slc_llama *m, Program &p, uint32_t ids_buf, uint32_t pos_buf) {
         }
         p.ready.push_back(std::move(rd));
     }
+    p.src_flat.clear();
+    p.src_count.clear();
+    for (const Ready &r : p.ready) {
+        p.src_count.push_back((uint32_t)r.scalar_src.size());
+        p.src_flat.insert(p.src_flat.end(), r.scalar_src.begin(), r.scalar_src.end());
+    }
+    p.memo = StepMemo{};
 }
 
 int fail(slc_llama *m, int status, const char *msg) {
@@ -457,6 +472,8 @@ extern "C" int slc_llama_create(slc_device *d, const slc_llama_config *cfg, slc_
     m->dev = d;
     m->cfg = c;
     m->cfg.tp_world = world;
+    const char *memo_env = getenv("SLC_STEP_MEMO");
+    m->memo = !(memo_env && strcmp(memo_env, "0") == 0);
     m->hq = c.heads / world;
     m->hkv = c.kv_heads / world;
     m->inter = c.inter / world;
@@ -627,15 +644,27 @@ extern "C" int slc_llama_step(slc_llama *m, int mode, const uint32_t *ids,
     // and the events bracket device work only; host-side dispatch cost shows
     // in the caller's wall clock.
     const bool deferred = d->capture != nullptr;
-    if (!deferred) cudaEventRecord(m->ev_begin, d->stream);
-    for (const Ready &r : p.ready) {
-        for (size_t i = 0; i < r.scalar_src.size(); i++) sc[i] = scalars_src[r.scalar_src[i]];
-        rc = slc_dispatch(d, &r.op, r.in.data(), r.iv.data(), r.in.size(), r.out.data(),
-                          r.ov.data(), r.out.size(), sc, r.scalar_src.size());
+    if (deferred && m->memo && capture_memo_valid(d, &p.memo)) {
+        // The program's commands replay as one known graph: relaunch it with
+        // this step's scalars instead of dispatching every command again
+        // (the checks above are the ones the scalars get at dispatch).
+        cudaEventRecord(m->ev_begin, d->stream);
+        if ((rc = capture_memo_replay(d, &p.memo, scalars_src, 2)) != SLC_OK) return rc;
+        m->memo_steps++;
+    } else {
+        if (!deferred) cudaEventRecord(m->ev_begin, d->stream);
+        for (const Ready &r : p.ready) {
+            for (size_t i = 0; i < r.scalar_src.size(); i++) sc[i] = scalars_src[r.scalar_src[i]];
+            rc = slc_dispatch(d, &r.op, r.in.data(), r.iv.data(), r.in.size(), r.out.data(),
+                              r.ov.data(), r.out.size(), sc, r.scalar_src.size());
+            if (rc != SLC_OK) return rc;
+        }
+        if (deferred) cudaEventRecord(m->ev_begin, d->stream);
+        rc = deferred && m->memo ? capture_flush_memo(d, &p.memo, p.src_flat.data(),
+                                                      p.src_count.data(), p.ready.size())
+                                 : slc_flush(d);
         if (rc != SLC_OK) return rc;
     }
-    if (deferred) cudaEventRecord(m->ev_begin, d->stream);
-    if ((rc = slc_flush(d)) != SLC_OK) return rc;
     cudaEventRecord(m->ev_end, d->stream);
     if ((rc = slc_synchronize(d)) != SLC_OK) return rc;
     cudaEventElapsedTime(&m->last_step_ms, m->ev_begin, m->ev_end);
@@ -684,6 +713,12 @@ extern "C" int slc_llama_kv_buffer(const slc_llama *m, uint32_t *buffer, uint64_
     if (!m) return SLC_ERR_EXECUTION;
     if (buffer) *buffer = m->kv;
     if (elements) *elements = m->decode.refs[m->decode.kv].len;
+    return SLC_OK;
+}
+
+extern "C" int slc_llama_memo_steps(const slc_llama *m, uint64_t *count) {
+    if (!m || !count) return SLC_ERR_EXECUTION;
+    *count = m->memo_steps;
     return SLC_OK;
 }
 

@@ -119,6 +119,7 @@ def _bind(lib):
         "slc_llama_weight_bytes": (C.c_int, [P, C.POINTER(C.c_uint64)]),
         "slc_llama_weight_ref": (C.c_int, [P, C.c_int, C.c_uint32, P, P]),
         "slc_llama_last_step_ms": (C.c_int, [P, C.POINTER(C.c_float)]),
+        "slc_llama_memo_steps": (C.c_int, [P, C.POINTER(C.c_uint64)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -220,3 +221,9 @@ class Llama:
         ms = C.c_float()
         self._check(self._lib.slc_llama_last_step_ms(self._m, C.byref(ms)))
         return float(ms.value)
+
+    def memo_steps(self) -> int:
+        """Steps that relaunched their program's captured graph directly."""
+        n = C.c_uint64()
+        self._check(self._lib.slc_llama_memo_steps(self._m, C.byref(n)))
+        return int(n.value)

@@ -30,6 +30,7 @@ def _fake_nvml(clocks, reasons):
 
 def _sample(nv, seconds=0.08):
     c = bench.ClockSampler(0)
+    c._nv, c._h = nv, None
     c._stop = threading.Event()
     c.thread = threading.Thread(target=c._nvml_loop, args=(nv, None, c._stop))
     c.thread.start()
@@ -60,6 +61,19 @@ def test_ordinal_maps_through_cuda_visible_devices(monkeypatch):
     assert bench.ClockSampler(0).index == 0
     monkeypatch.delenv("CUDA_VISIBLE_DEVICES")
     assert bench.ClockSampler(2).index == 2
+
+
+def test_region_end_is_sampled_even_if_the_thread_took_none():
+    # The sample taken by stop() itself: a region shorter than the thread's
+    # first poll still gets a record.
+    nv = _fake_nvml([1965], 0x4)
+    c = bench.ClockSampler(0)
+    c._nv, c._h = nv, None
+    c._stop = threading.Event()
+    c.thread = threading.Thread(target=lambda: None)
+    c.thread.start()
+    rec = c.stop()
+    assert rec["samples"] == 1 and rec["sm_mhz"] == 1965 and rec["reasons"] == ["sw_power_cap"]
 
 
 def test_no_sources_give_no_record():
