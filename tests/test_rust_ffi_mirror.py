@@ -205,3 +205,11 @@ def test_constants_match_the_header():
                                     ("SlcBufferRef", "slc_buffer_ref weights")])
 def test_kind_mapping(rust, c):
     assert _rust_kind(rust) == _c_kind(c)
+
+
+def test_lib_uses_only_names_the_ffi_declares():
+    lib = _strip_comments(open(os.path.join(os.path.dirname(FFI), "lib.rs")).read())
+    src = _rust_source()
+    declared = set(re.findall(r"pub (?:fn|struct|const) (\w+)", src))
+    used = set(re.findall(r"ffi::(\w+)", lib))
+    assert used and used <= declared, sorted(used - declared)
