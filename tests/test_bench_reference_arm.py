@@ -1,0 +1,35 @@
+"""The benchmark's reference arm on CPU (it needs no GPU): `bench.py --impl
+reference` times the restated reference kernels on the host's cores and
+prints one JSON line with the same metric, unit, config workload and
+direction as the GPU arm, marked `"impl": "reference"`, with a
+`cpu_baseline` describing the run and an `e2e` equal to its own value with
+no host-device bytes."""
+import json
+import os
+import subprocess
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_reference_arm_prints_one_contract_line():
+    env = dict(os.environ, OMP_NUM_THREADS="2")
+    out = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference",
+                          "--steps", "1", "--warmup", "0"], cwd=ROOT, env=env,
+                         capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip().startswith("{")]
+    assert len(lines) == 1, out.stdout
+    d = json.loads(lines[0])
+    import bench
+    assert d["impl"] == "reference"
+    assert d["metric"] == bench.METRIC and d["unit"] == "tok/s"
+    assert d["higher_is_better"] is True and d["n_gpus"] == 1
+    assert d["steps"] == 1 and d["warmup"] == 0
+    assert d["config"]["workload"] == "llama3-8b-int4-decode"
+    assert d["value"] > 0 and d["ms_per_step"] > 0
+    cb = d["cpu_baseline"]
+    assert cb["value"] == d["value"] and cb["kind"] in ("port", "reference") and cb["cores"] >= 1
+    assert cb["sample"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
